@@ -1,0 +1,1230 @@
+// engine.cu -- host runtime of libacmcuda.so and the C ABI (include/acm.h).
+//
+// A model holds the GGUF tensors exactly as uploaded, fp32 norm/bias vectors,
+// the RoPE cos/sin table, a paged fp32 KV cache shared by `max_seqs`
+// sequence slots, and activation buffers for up to TMAX tokens per pass.
+// Every pass runs a batch of tokens; each token carries (slot, position), so a
+// prefill chunk (one slot, consecutive positions) and a batched decode step
+// (many slots, one token each) go through the same kernels.  Decode steps of
+// a fixed batch size are captured once into a CUDA graph and replayed; the
+// graph reads its token ids and positions from device memory and ends with a
+// kernel that advances them, so the token loop can run on the device without
+// a host round trip per token.
+#include <fcntl.h>
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <map>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "acm.h"
+#include "gguf_host.h"
+#include "kernels.h"
+#include "quant.cuh"
+
+using namespace acm;
+
+std::atomic<unsigned long long> acm::g_kernel_launches{0};
+
+namespace {
+
+constexpr int TMAX = 1024;        // tokens per pass (the reference's prefill chunk, sampler.go:116)
+constexpr int PAGE = 64;          // KV positions per page
+constexpr int NSPLIT_MAX = 32;
+constexpr int PART_TOKSPLIT = 4096;
+constexpr int HIST_MAX = 64;      // decode steps per device-side chunk
+
+std::string fmt(const char *f, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, f);
+    vsnprintf(buf, sizeof buf, f, ap);
+    va_end(ap);
+    return buf;
+}
+
+}  // namespace
+
+struct acm_engine {
+    int device = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    void *scratch = nullptr;
+    size_t scratch_bytes = 0;
+};
+
+namespace {
+
+struct DevTensor {
+    std::string name;
+    uint32_t type = 0;
+    std::vector<uint64_t> dims;
+    int64_t numel = 0;
+    size_t nbytes = 0;
+    uint8_t *d = nullptr;
+    int64_t k() const { return dims.empty() ? numel : (int64_t)dims[0]; }
+    int64_t rows() const { return dims.size() < 2 ? 1 : numel / (int64_t)dims[0]; }
+};
+
+struct Layer {
+    DevTensor *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr, *gate = nullptr, *up = nullptr,
+              *down = nullptr;
+    float *attn_nw = nullptr, *ffn_nw = nullptr, *q_nw = nullptr, *k_nw = nullptr;
+    float *q_b = nullptr, *k_b = nullptr, *v_b = nullptr;
+};
+
+struct Seq {
+    bool open = false;
+    int pos = 0;
+    std::vector<int> pages;
+};
+
+template <typename T>
+struct Pinned {
+    T *p = nullptr;
+    size_t n = 0;
+    cudaError_t alloc(size_t cnt) {
+        n = cnt;
+        return cudaMallocHost(reinterpret_cast<void **>(&p), sizeof(T) * std::max<size_t>(cnt, 1));
+    }
+    void release() {
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+    }
+};
+
+}  // namespace
+
+struct acm_model {
+    acm_engine *e = nullptr;
+    acm_config c{};
+    int max_seqs = 1;
+    std::string err;
+    std::unordered_map<std::string, DevTensor> tensors;
+    std::vector<void *> allocs;
+    bool finalized = false;
+
+    DevTensor *embd = nullptr, *out = nullptr;
+    float *out_nw = nullptr;
+    std::vector<Layer> layers;
+    float2 *rope_tab = nullptr;
+
+    // paged KV cache
+    int max_pages = 0, n_pages = 0;
+    float *kpool = nullptr, *vpool = nullptr;
+    int64_t layer_stride = 0;
+    std::vector<int> free_pages;
+    int32_t *d_page_table = nullptr;
+    Pinned<int32_t> h_page_table;
+    std::vector<Seq> seqs;
+
+    // activations
+    int tdec = 8;  // largest decode batch (max(8, max_seqs))
+    float *x = nullptr, *h = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *hb = nullptr,
+          *hb2 = nullptr, *part = nullptr, *logits = nullptr;
+
+    // per-token metadata and sampler state (device + pinned staging)
+    int32_t *d_tok = nullptr, *d_seq = nullptr, *d_pos = nullptr, *d_out = nullptr, *d_topk = nullptr;
+    double *d_temp = nullptr, *d_topp = nullptr;
+    uint64_t *d_seed = nullptr, *d_step = nullptr, *d_cand = nullptr;
+    int32_t *d_hist = nullptr, *d_hist_col = nullptr;
+    int nchunks = 0;
+    Pinned<int32_t> h_tok, h_seq, h_pos, h_out, h_topk, h_hist;
+    Pinned<double> h_temp, h_topp;
+    Pinned<uint64_t> h_seed, h_step;
+
+    struct Graph {
+        cudaGraphExec_t exec = nullptr;
+        unsigned long long kernels = 0;  // kernel launches captured in the graph
+    };
+    std::map<std::pair<int, int>, Graph> graphs;
+    Graph gemv_bench;
+    cudaEvent_t ev[4] = {};
+    double last_prefill_s = 0, last_decode_s = 0;
+};
+
+namespace {
+
+int set_err(acm_model *m, int code, const std::string &msg) {
+    if (m) m->err = msg;
+    return code;
+}
+int set_eerr(acm_engine *e, int code, const std::string &msg) {
+    if (e) e->err = msg;
+    return code;
+}
+
+#define CK_M(call)                                                                                  \
+    do {                                                                                            \
+        cudaError_t e_ = (call);                                                                    \
+        if (e_ != cudaSuccess)                                                                      \
+            return set_err(m, e_ == cudaErrorMemoryAllocation ? ACM_ERR_OOM : ACM_ERR_CUDA,         \
+                           fmt("%s: %s", #call, cudaGetErrorString(e_)));                           \
+    } while (0)
+#define CK_E(call)                                                                                  \
+    do {                                                                                            \
+        cudaError_t e_ = (call);                                                                    \
+        if (e_ != cudaSuccess)                                                                      \
+            return set_eerr(e, e_ == cudaErrorMemoryAllocation ? ACM_ERR_OOM : ACM_ERR_CUDA,        \
+                            fmt("%s: %s", #call, cudaGetErrorString(e_)));                          \
+    } while (0)
+
+template <typename T>
+cudaError_t dalloc(acm_model *m, T **p, size_t count) {
+    void *v = nullptr;
+    cudaError_t e = cudaMalloc(&v, sizeof(T) * std::max<size_t>(count, 1));
+    if (e == cudaSuccess) {
+        m->allocs.push_back(v);
+        *p = static_cast<T *>(v);
+    }
+    return e;
+}
+
+// Synchronise the model stream and turn device-side error flags into status.
+int sync_check(acm_model *m) {
+    cudaError_t e = cudaStreamSynchronize(m->e->stream);
+    if (e != cudaSuccess) return set_err(m, ACM_ERR_CUDA, fmt("device error: %s", cudaGetErrorString(e)));
+    const int de = read_and_clear_dev_error();
+    if (de == DEV_ERR_TIMEOUT) return set_err(m, ACM_ERR_TIMEOUT, "a device-side wait timed out");
+    if (de == DEV_ERR_BOUNDS) return set_err(m, ACM_ERR_INVALID, "token id out of range (device check)");
+    return ACM_OK;
+}
+
+int ensure_pages(acm_model *m, int seq, int upto) {
+    Seq &s = m->seqs[seq];
+    const int need = (upto + PAGE - 1) / PAGE;
+    if (need > m->max_pages) return set_err(m, ACM_ERR_CTX_EXCEEDED, "context length exceeded");
+    bool dirty = false;
+    while ((int)s.pages.size() < need) {
+        if (m->free_pages.empty()) return set_err(m, ACM_ERR_OOM, "KV cache pages exhausted");
+        const int pg = m->free_pages.back();
+        m->free_pages.pop_back();
+        m->h_page_table.p[(size_t)seq * m->max_pages + s.pages.size()] = pg;
+        s.pages.push_back(pg);
+        dirty = true;
+    }
+    if (dirty) {
+        CK_M(cudaMemcpyAsync(m->d_page_table + (size_t)seq * m->max_pages,
+                             m->h_page_table.p + (size_t)seq * m->max_pages, sizeof(int32_t) * m->max_pages,
+                             cudaMemcpyHostToDevice, m->e->stream));
+    }
+    return ACM_OK;
+}
+
+int attn_nsplit(acm_model *m, int ntok, int max_pos) {
+    const int nkv = m->c.n_head_kv;
+    if ((int64_t)ntok * nkv >= 2 * m->e->num_sms) return 1;
+    int ns = (2 * m->e->num_sms + ntok * nkv - 1) / (ntok * nkv);
+    ns = std::min(ns, NSPLIT_MAX);
+    ns = std::min(ns, std::max(1, (max_pos + 1 + 15) / 16));
+    ns = std::min(ns, std::max(1, PART_TOKSPLIT / ntok));
+    return std::max(ns, 1);
+}
+
+// One pass over `ntok` tokens whose ids/slots/positions are already in
+// d_tok/d_seq/d_pos.  Logits are produced for tokens [lm_first, lm_first +
+// lm_count) into their slots' rows of m->logits.  Enqueues only (capturable).
+int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count) {
+    const acm_config &c = m->c;
+    cudaStream_t st = m->e->stream;
+    const int E = c.n_embd, hd = c.head_dim, qd = c.n_head * hd, kvd = c.n_head_kv * hd, F = c.n_ff;
+    const int S = m->e->num_sms;
+    const float eps = c.rms_eps;
+    CK_M(dequant_launch(m->embd->type, m->embd->d, E, ntok, m->d_tok, m->embd->rows(), m->x, E, st));
+    KVDesc kv{m->kpool, m->vpool, m->d_page_table, m->max_pages, PAGE, m->layer_stride, kvd};
+    TokMeta tm{m->d_seq, m->d_pos};
+    const float scale = 1.0f / (float)sqrt((double)hd);
+    const int nsplit = attn_nsplit(m, ntok, max_pos);
+    for (int l = 0; l < c.n_layers; l++) {
+        const Layer &L = m->layers[l];
+        // q, k, v (+ bias) from RMSNorm(x)
+        const bool gv = gemv_supported(L.q->type, E, ntok) && gemv_supported(L.k->type, E, ntok) &&
+                        gemv_supported(L.v->type, E, ntok);
+        if (gv) {
+            GemvSegDesc sg[3] = {{L.q->d, nullptr, (int)L.q->type, qd, EPI_STORE, m->q, qd, L.q_b, nullptr},
+                                 {L.k->d, nullptr, (int)L.k->type, kvd, EPI_STORE, m->k, kvd, L.k_b, nullptr},
+                                 {L.v->d, nullptr, (int)L.v->type, kvd, EPI_STORE, m->v, kvd, L.v_b, nullptr}};
+            CK_M(gemv_launch(sg, 3, m->x, E, E, ntok, L.attn_nw, eps, S, st));
+        } else {
+            CK_M(rmsnorm_launch(m->x, E, L.attn_nw, m->h, E, ntok, E, eps, st));
+            CK_M(gemm_launch({L.q->d, nullptr, (int)L.q->type, qd, E, ntok, m->h, E, m->q, qd, EPI_STORE, L.q_b, nullptr}, st));
+            CK_M(gemm_launch({L.k->d, nullptr, (int)L.k->type, kvd, E, ntok, m->h, E, m->k, kvd, EPI_STORE, L.k_b, nullptr}, st));
+            CK_M(gemm_launch({L.v->d, nullptr, (int)L.v->type, kvd, E, ntok, m->h, E, m->v, kvd, EPI_STORE, L.v_b, nullptr}, st));
+        }
+        RopeDesc rd{m->q, m->k, m->v, L.q_nw, L.k_nw, m->rope_tab, c.n_head, c.n_head_kv, hd, c.rope_dim,
+                    c.rope_interleaved, eps};
+        CK_M(rope_append_launch(rd, kv, l, tm, ntok, st));
+        AttnDesc ad{m->q, m->att, c.n_head, c.n_head_kv, hd, scale, m->part, nsplit};
+        CK_M(attention_launch(ad, kv, l, tm, ntok, max_pos, st));
+        // x += Wo att
+        if (gemv_supported(L.o->type, qd, ntok)) {
+            GemvSegDesc so{L.o->d, nullptr, (int)L.o->type, E, EPI_ADD, m->x, E, nullptr, nullptr};
+            CK_M(gemv_launch(&so, 1, m->att, qd, qd, ntok, nullptr, eps, S, st));
+        } else {
+            CK_M(gemm_launch({L.o->d, nullptr, (int)L.o->type, E, qd, ntok, m->att, qd, m->x, E, EPI_ADD, nullptr, nullptr}, st));
+        }
+        // hb = silu(Wg h) * (Wu h), h = RMSNorm(x)
+        const bool pair = L.gate->type == L.up->type;
+        if (gemv_supported(L.gate->type, E, ntok) && gemv_supported(L.up->type, E, ntok)) {
+            if (pair) {
+                GemvSegDesc sf{L.gate->d, L.up->d, (int)L.gate->type, F, EPI_SWIGLU, m->hb, F, nullptr, nullptr};
+                CK_M(gemv_launch(&sf, 1, m->x, E, E, ntok, L.ffn_nw, eps, S, st));
+            } else {
+                GemvSegDesc sf[2] = {{L.gate->d, nullptr, (int)L.gate->type, F, EPI_STORE, m->hb, F, nullptr, nullptr},
+                                     {L.up->d, nullptr, (int)L.up->type, F, EPI_STORE, m->hb2, F, nullptr, nullptr}};
+                CK_M(gemv_launch(sf, 2, m->x, E, E, ntok, L.ffn_nw, eps, S, st));
+                CK_M(swiglu_launch(m->hb, m->hb2, m->hb, (int64_t)ntok * F, st));
+            }
+        } else {
+            CK_M(rmsnorm_launch(m->x, E, L.ffn_nw, m->h, E, ntok, E, eps, st));
+            if (pair) {
+                CK_M(gemm_launch({L.gate->d, L.up->d, (int)L.gate->type, F, E, ntok, m->h, E, m->hb, F, EPI_SWIGLU, nullptr, nullptr}, st));
+            } else {
+                CK_M(gemm_launch({L.gate->d, nullptr, (int)L.gate->type, F, E, ntok, m->h, E, m->hb, F, EPI_STORE, nullptr, nullptr}, st));
+                CK_M(gemm_launch({L.up->d, nullptr, (int)L.up->type, F, E, ntok, m->h, E, m->hb2, F, EPI_STORE, nullptr, nullptr}, st));
+                CK_M(swiglu_launch(m->hb, m->hb2, m->hb, (int64_t)ntok * F, st));
+            }
+        }
+        // x += Wd hb
+        if (gemv_supported(L.down->type, F, ntok)) {
+            GemvSegDesc sd{L.down->d, nullptr, (int)L.down->type, E, EPI_ADD, m->x, E, nullptr, nullptr};
+            CK_M(gemv_launch(&sd, 1, m->hb, F, F, ntok, nullptr, eps, S, st));
+        } else {
+            CK_M(gemm_launch({L.down->d, nullptr, (int)L.down->type, E, F, ntok, m->hb, F, m->x, E, EPI_ADD, nullptr, nullptr}, st));
+        }
+    }
+    if (lm_count > 0) {
+        // final RMSNorm + lm_head for the requested tokens, into their slots' logits rows
+        const float *xin = m->x + (size_t)lm_first * E;
+        const int V = (int)m->out->rows();
+        if (gemv_supported(m->out->type, E, lm_count)) {
+            GemvSegDesc so{m->out->d, nullptr, (int)m->out->type, V, EPI_STORE, m->logits, c.vocab, nullptr,
+                           m->d_seq + lm_first};
+            CK_M(gemv_launch(&so, 1, xin, E, E, lm_count, m->out_nw, eps, S, st));
+        } else {
+            CK_M(rmsnorm_launch(xin, E, m->out_nw, m->h, E, lm_count, E, eps, st));
+            CK_M(gemm_launch({m->out->d, nullptr, (int)m->out->type, V, E, lm_count, m->h, E, m->logits, c.vocab,
+                              EPI_STORE, nullptr, m->d_seq + lm_first}, st));
+        }
+    }
+    return ACM_OK;
+}
+
+int sample_pass(acm_model *m, int ntok, bool greedy) {
+    SampleDesc sd{m->logits, m->d_seq, m->c.vocab, m->c.vocab, m->d_temp, m->d_topk, m->d_topp, m->d_seed,
+                  m->d_step, m->d_out, m->d_cand, m->nchunks};
+    CK_M(sample_launch(sd, ntok, greedy, m->e->stream));
+    return ACM_OK;
+}
+
+// Upload ids/slots/positions of a token batch from the pinned staging.
+int upload_meta(acm_model *m, int ntok) {
+    cudaStream_t st = m->e->stream;
+    CK_M(cudaMemcpyAsync(m->d_tok, m->h_tok.p, sizeof(int32_t) * ntok, cudaMemcpyHostToDevice, st));
+    CK_M(cudaMemcpyAsync(m->d_seq, m->h_seq.p, sizeof(int32_t) * ntok, cudaMemcpyHostToDevice, st));
+    CK_M(cudaMemcpyAsync(m->d_pos, m->h_pos.p, sizeof(int32_t) * ntok, cudaMemcpyHostToDevice, st));
+    return ACM_OK;
+}
+
+int upload_sampler(acm_model *m, int ntok) {
+    cudaStream_t st = m->e->stream;
+    CK_M(cudaMemcpyAsync(m->d_temp, m->h_temp.p, sizeof(double) * ntok, cudaMemcpyHostToDevice, st));
+    CK_M(cudaMemcpyAsync(m->d_topp, m->h_topp.p, sizeof(double) * ntok, cudaMemcpyHostToDevice, st));
+    CK_M(cudaMemcpyAsync(m->d_topk, m->h_topk.p, sizeof(int32_t) * ntok, cudaMemcpyHostToDevice, st));
+    CK_M(cudaMemcpyAsync(m->d_seed, m->h_seed.p, sizeof(uint64_t) * ntok, cudaMemcpyHostToDevice, st));
+    CK_M(cudaMemcpyAsync(m->d_step, m->h_step.p, sizeof(uint64_t) * ntok, cudaMemcpyHostToDevice, st));
+    return ACM_OK;
+}
+
+// A decode step for `ntok` tokens: forward + sample + advance, replayed from
+// a CUDA graph captured on first use for this (batch size, greedy) pair.
+int decode_graph_launch(acm_model *m, int ntok, bool greedy) {
+    const auto key = std::make_pair(ntok, greedy ? 1 : 0);
+    auto it = m->graphs.find(key);
+    cudaStream_t st = m->e->stream;
+    if (it == m->graphs.end()) {
+        // warm-up run outside capture (first launches set kernel attributes)
+        int rc = forward_pass(m, ntok, m->c.max_ctx - 1, 0, ntok);
+        if (rc) return rc;
+        if ((rc = sample_pass(m, ntok, greedy))) return rc;
+        if ((rc = sync_check(m))) return rc;
+        cudaGraph_t g = nullptr;
+        const unsigned long long before = g_kernel_launches.load();
+        CK_M(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        rc = forward_pass(m, ntok, m->c.max_ctx - 1, 0, ntok);
+        if (!rc) rc = sample_pass(m, ntok, greedy);
+        cudaError_t ae = advance_launch(m->d_tok, m->d_pos, m->d_step, m->d_out, m->d_hist, HIST_MAX, m->d_hist_col,
+                                        ntok, st);
+        cudaError_t ce = cudaStreamEndCapture(st, &g);
+        const unsigned long long captured = g_kernel_launches.load() - before;
+        g_kernel_launches -= captured;  // capturing is not executing
+        if (rc) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (ae != cudaSuccess || ce != cudaSuccess) {
+            if (g) cudaGraphDestroy(g);
+            return set_err(m, ACM_ERR_CUDA, fmt("graph capture failed: %s", cudaGetErrorString(ae ? ae : ce)));
+        }
+        cudaGraphExec_t ex = nullptr;
+        cudaError_t ie = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        if (ie != cudaSuccess) return set_err(m, ACM_ERR_CUDA, fmt("graph instantiate: %s", cudaGetErrorString(ie)));
+        acm_model::Graph gr;
+        gr.exec = ex;
+        gr.kernels = captured;
+        it = m->graphs.emplace(key, gr).first;
+        // the warm-up pass above advanced nothing on the device; restore inputs
+        int rc2 = upload_meta(m, ntok);
+        if (rc2) return rc2;
+        if ((rc2 = upload_sampler(m, ntok))) return rc2;
+    }
+    CK_M(cudaGraphLaunch(it->second.exec, st));
+    g_kernel_launches += it->second.kernels;
+    return ACM_OK;
+}
+
+int check_seq(acm_model *m, int seq) {
+    if (!m || !m->finalized) return set_err(m, ACM_ERR_INVALID, "model not finalized");
+    if (seq < 0 || seq >= m->max_seqs || !m->seqs[seq].open) return set_err(m, ACM_ERR_NO_SEQ, fmt("sequence %d is not open", seq));
+    return ACM_OK;
+}
+
+void fill_sampler(acm_model *m, int t, const acm_sampler *s, uint64_t step) {
+    m->h_temp.p[t] = s ? s->temp : 0.0;
+    m->h_topk.p[t] = s ? s->top_k : 0;
+    m->h_topp.p[t] = s ? s->top_p : 0.0;
+    m->h_seed.p[t] = s ? s->seed : 0;
+    m->h_step.p[t] = step;
+}
+
+double ev_seconds(cudaEvent_t a, cudaEvent_t b) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, a, b);
+    return ms * 1e-3;
+}
+
+// Forward over n tokens of one sequence (chunks of TMAX), logits of the last
+// token into the slot's row.  Caller has validated the context length.
+int forward_seq(acm_model *m, int seq, const int32_t *toks, int n) {
+    Seq &s = m->seqs[seq];
+    int rc;
+    if ((rc = ensure_pages(m, seq, s.pos + n))) return rc;
+    for (int i = 0; i < n; i += TMAX) {
+        const int cnt = std::min(TMAX, n - i);
+        if (i > 0 && (rc = sync_check(m))) return rc;  // staging reuse
+        for (int j = 0; j < cnt; j++) {
+            m->h_tok.p[j] = toks[i + j];
+            m->h_seq.p[j] = seq;
+            m->h_pos.p[j] = s.pos + i + j;
+        }
+        if ((rc = upload_meta(m, cnt))) return rc;
+        const bool last = i + cnt == n;
+        if ((rc = forward_pass(m, cnt, s.pos + i + cnt - 1, cnt - 1, last ? 1 : 0))) return rc;
+    }
+    s.pos += n;
+    return ACM_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+ACM_API const char *acm_version(void) { return "acm-b200 0.1 (sm_100a)"; }
+
+ACM_API int acm_open(int device, acm_engine **out) {
+    if (!out) return ACM_ERR_INVALID;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return ACM_ERR_CUDA;
+    auto *e = new acm_engine();
+    e->device = device;
+    cudaError_t ce = cudaSetDevice(device);
+    if (ce == cudaSuccess) ce = cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, device);
+    if (ce == cudaSuccess) ce = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
+    if (ce != cudaSuccess) {
+        delete e;
+        return ACM_ERR_CUDA;
+    }
+    *out = e;
+    return ACM_OK;
+}
+
+ACM_API int acm_close(acm_engine *e) {
+    if (!e) return ACM_ERR_INVALID;
+    cudaSetDevice(e->device);
+    if (e->scratch) cudaFree(e->scratch);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+    return ACM_OK;
+}
+
+ACM_API const char *acm_engine_error(acm_engine *e) { return e ? e->err.c_str() : "null engine"; }
+ACM_API void *acm_engine_stream(acm_engine *e) { return e ? (void *)e->stream : nullptr; }
+ACM_API int acm_engine_sync(acm_engine *e) {
+    if (!e) return ACM_ERR_INVALID;
+    cudaSetDevice(e->device);
+    CK_E(cudaStreamSynchronize(e->stream));
+    return ACM_OK;
+}
+
+ACM_API int acm_model_create(acm_engine *e, const acm_config *cfg, int32_t max_seqs, acm_model **out) {
+    if (!e || !cfg || !out || max_seqs < 1 || max_seqs > 1024) return ACM_ERR_INVALID;
+    *out = nullptr;
+    const acm_config &c = *cfg;
+    if (c.n_layers <= 0 || c.n_embd <= 0 || c.n_head <= 0 || c.n_head_kv <= 0 || c.head_dim <= 0 || c.n_ff <= 0 ||
+        c.vocab <= 0 || c.max_ctx <= 0)
+        return set_eerr(e, ACM_ERR_INVALID, "invalid model configuration");
+    if (c.arch < 0 || c.arch > 2) return set_eerr(e, ACM_ERR_UNSUPPORTED_ARCH, "unsupported architecture");
+    auto *m = new acm_model();
+    m->e = e;
+    m->c = c;
+    m->max_seqs = max_seqs;
+    *out = m;
+    return ACM_OK;
+}
+
+ACM_API int acm_model_add_tensor(acm_model *m, const char *name, uint32_t ggml_type, const uint64_t *dims,
+                                 int32_t ndims, const void *host_bytes, size_t nbytes) {
+    if (!m || !name || (ndims > 0 && !dims) || ndims < 0 || ndims > 8 || (!host_bytes && nbytes))
+        return set_err(m, ACM_ERR_INVALID, "invalid tensor arguments");
+    if (m->finalized) return set_err(m, ACM_ERR_INVALID, "model already finalized");
+    if (!type_ok((int)ggml_type))
+        return set_err(m, ACM_ERR_UNSUPPORTED_TYPE, fmt("tensor %s: unsupported type %u", name, ggml_type));
+    DevTensor t;
+    t.name = name;
+    t.type = ggml_type;
+    t.numel = 1;
+    for (int i = 0; i < ndims; i++) {
+        t.dims.push_back(dims[i]);
+        t.numel *= (int64_t)dims[i];
+    }
+    const int be = blk_elems((int)ggml_type);
+    if (ndims == 0 || t.numel <= 0 || t.dims[0] % be)
+        return set_err(m, ACM_ERR_INVALID, fmt("tensor %s: bad shape", name));
+    t.nbytes = (size_t)(t.numel / be) * blk_bytes((int)ggml_type);
+    if (nbytes != t.nbytes)
+        return set_err(m, ACM_ERR_INVALID, fmt("tensor %s: %zu bytes given, %zu expected", name, nbytes, t.nbytes));
+    cudaSetDevice(m->e->device);
+    // 16 bytes of padding: the bulk copies round spans up to 16 bytes and the
+    // unaligned word loader reads one word past a run
+    CK_M(dalloc(m, &t.d, t.nbytes + 64));
+    CK_M(cudaMemcpy(t.d, host_bytes, t.nbytes, cudaMemcpyHostToDevice));
+    CK_M(cudaMemset(t.d + t.nbytes, 0, 64));
+    m->tensors[name] = std::move(t);
+    return ACM_OK;
+}
+
+static int norm_vec(acm_model *m, const DevTensor *t, int64_t n, float **out, const char *what) {
+    *out = nullptr;
+    if (!t) return ACM_OK;
+    if (t->numel != n) return set_err(m, ACM_ERR_INVALID, fmt("%s: %lld elements, %lld expected", what,
+                                                              (long long)t->numel, (long long)n));
+    CK_M(dalloc(m, out, (size_t)n + 4));
+    if (n % 32 == 0) {
+        CK_M(dequant_launch((int)t->type, t->d, n, 1, nullptr, 1, *out, n, m->e->stream));
+    } else {
+        // short vectors not a multiple of 32 elements: F32 only
+        if (t->type != T_F32) return set_err(m, ACM_ERR_UNSUPPORTED_TYPE, fmt("%s: unsupported type", what));
+        CK_M(cudaMemcpyAsync(*out, t->d, sizeof(float) * n, cudaMemcpyDeviceToDevice, m->e->stream));
+    }
+    return ACM_OK;
+}
+
+ACM_API int acm_model_finalize(acm_model *m) {
+    if (!m) return ACM_ERR_INVALID;
+    if (m->finalized) return set_err(m, ACM_ERR_INVALID, "model already finalized");
+    cudaSetDevice(m->e->device);
+    acm_config &c = m->c;
+    auto get = [&](const std::string &n) -> DevTensor * {
+        auto it = m->tensors.find(n);
+        return it == m->tensors.end() ? nullptr : &it->second;
+    };
+    const int E = c.n_embd, hd = c.head_dim, qd = c.n_head * hd, kvd = c.n_head_kv * hd, F = c.n_ff;
+    if (c.n_head % c.n_head_kv || c.n_head / c.n_head_kv > 8)
+        return set_err(m, ACM_ERR_INVALID, "unsupported head grouping");
+    if (hd != 64 && hd != 128) return set_err(m, ACM_ERR_INVALID, fmt("unsupported head_dim %d", hd));
+    if (c.rope_dim <= 0 || c.rope_dim > hd || c.rope_dim % 2)
+        return set_err(m, ACM_ERR_INVALID, fmt("unsupported rope dimension %d", c.rope_dim));
+    // model.go:161-169
+    m->embd = get("token_embd.weight");
+    m->out = get("output.weight");
+    DevTensor *on = get("output_norm.weight");
+    if (!m->embd || !on) return set_err(m, ACM_ERR_MISSING_TENSOR, "missing embedding or output norm tensors");
+    if (!m->out) m->out = m->embd;
+    int rc;
+    if ((rc = norm_vec(m, on, E, &m->out_nw, "output_norm.weight"))) return rc;
+    auto shape_ok = [&](const DevTensor *t, int64_t k, int64_t n) { return t->k() == k && t->rows() == n; };
+    if (m->embd->k() != E) return set_err(m, ACM_ERR_INVALID, "token_embd.weight: bad shape");
+    if (m->out->k() != E || m->out->rows() != c.vocab)
+        return set_err(m, ACM_ERR_INVALID, "output tensor rows do not match the token list");
+    m->layers.assign(c.n_layers, Layer());
+    for (int i = 0; i < c.n_layers; i++) {
+        const std::string b = "blk." + std::to_string(i) + ".";
+        Layer &L = m->layers[i];
+        L.q = get(b + "attn_q.weight");
+        L.k = get(b + "attn_k.weight");
+        L.v = get(b + "attn_v.weight");
+        L.o = get(b + "attn_output.weight");
+        L.gate = get(b + "ffn_gate.weight");
+        L.up = get(b + "ffn_up.weight");
+        L.down = get(b + "ffn_down.weight");
+        DevTensor *an = get(b + "attn_norm.weight"), *fn = get(b + "ffn_norm.weight");
+        if (!an || !L.q || !L.k || !L.v || !L.o || !fn || !L.gate || !L.up || !L.down)
+            return set_err(m, ACM_ERR_MISSING_TENSOR, fmt("layer %d: missing tensors", i));  // model.go:196-199
+        if (!shape_ok(L.q, E, qd) || !shape_ok(L.k, E, kvd) || !shape_ok(L.v, E, kvd) || !shape_ok(L.o, qd, E) ||
+            !shape_ok(L.gate, E, F) || !shape_ok(L.up, E, F) || !shape_ok(L.down, F, E))
+            return set_err(m, ACM_ERR_INVALID, fmt("layer %d: tensor shapes do not match the configuration", i));
+        if ((rc = norm_vec(m, an, E, &L.attn_nw, "attn_norm"))) return rc;
+        if ((rc = norm_vec(m, fn, E, &L.ffn_nw, "ffn_norm"))) return rc;
+        if ((rc = norm_vec(m, get(b + "attn_q_norm.weight"), hd, &L.q_nw, "attn_q_norm"))) return rc;
+        if ((rc = norm_vec(m, get(b + "attn_k_norm.weight"), hd, &L.k_nw, "attn_k_norm"))) return rc;
+        if ((rc = norm_vec(m, get(b + "attn_q.bias"), qd, &L.q_b, "attn_q.bias"))) return rc;
+        if ((rc = norm_vec(m, get(b + "attn_k.bias"), kvd, &L.k_b, "attn_k.bias"))) return rc;
+        if ((rc = norm_vec(m, get(b + "attn_v.bias"), kvd, &L.v_b, "attn_v.bias"))) return rc;
+    }
+    // RoPE table: ropeFreqs (model.go:253-280) then cos/sin per position as
+    // rope() computes them (model.go:240): float32(cos(float64(float32(pos)*f)))
+    {
+        const int half = c.rope_dim / 2;
+        std::vector<float> f(half);
+        for (int i = 0; i < half; i++) f[i] = 1.0f / (float)pow((double)c.rope_base, (double)(2 * i) / (double)c.rope_dim);
+        if (c.rope_scaling == ACM_ROPE_LINEAR) {
+            for (int i = 0; i < half; i++) f[i] /= c.rope_factor;
+        } else if (c.rope_scaling == ACM_ROPE_LLAMA3) {
+            const float lo_wl = c.rope_orig_ctx / c.rope_lo_f, hi_wl = c.rope_orig_ctx / c.rope_hi_f;
+            for (int i = 0; i < half; i++) {
+                const double wl = 2 * M_PI / (double)f[i];
+                if (wl < (double)hi_wl) {
+                } else if (wl > (double)lo_wl) {
+                    f[i] /= c.rope_factor;
+                } else {
+                    const float smooth = (c.rope_orig_ctx / (float)wl - c.rope_lo_f) / (c.rope_hi_f - c.rope_lo_f);
+                    f[i] = (1 - smooth) * f[i] / c.rope_factor + smooth * f[i];
+                }
+            }
+        }
+        std::vector<float2> tab((size_t)c.max_ctx * half);
+        for (int p = 0; p < c.max_ctx; p++)
+            for (int i = 0; i < half; i++) {
+                volatile float a = (float)p * f[i];
+                tab[(size_t)p * half + i] = make_float2((float)cos((double)a), (float)sin((double)a));
+            }
+        CK_M(dalloc(m, &m->rope_tab, tab.size()));
+        CK_M(cudaMemcpy(m->rope_tab, tab.data(), sizeof(float2) * tab.size(), cudaMemcpyHostToDevice));
+    }
+    // paged KV cache: enough pages for every slot at full context
+    m->max_pages = (c.max_ctx + PAGE - 1) / PAGE;
+    m->n_pages = m->max_pages * m->max_seqs;
+    m->layer_stride = (int64_t)m->n_pages * PAGE * kvd;
+    CK_M(dalloc(m, &m->kpool, (size_t)m->layer_stride * c.n_layers));
+    CK_M(dalloc(m, &m->vpool, (size_t)m->layer_stride * c.n_layers));
+    m->free_pages.clear();
+    for (int p = m->n_pages - 1; p >= 0; p--) m->free_pages.push_back(p);
+    CK_M(dalloc(m, &m->d_page_table, (size_t)m->max_seqs * m->max_pages));
+    CK_M(m->h_page_table.alloc((size_t)m->max_seqs * m->max_pages));
+    for (size_t i = 0; i < (size_t)m->max_seqs * m->max_pages; i++) m->h_page_table.p[i] = 0;
+    CK_M(cudaMemcpy(m->d_page_table, m->h_page_table.p, sizeof(int32_t) * m->max_seqs * m->max_pages,
+                    cudaMemcpyHostToDevice));
+    m->seqs.assign(m->max_seqs, Seq());
+    // activations
+    m->tdec = std::max(8, m->max_seqs);
+    const size_t T = (size_t)std::max(TMAX, m->tdec);
+    CK_M(dalloc(m, &m->x, T * E));
+    CK_M(dalloc(m, &m->h, T * E));
+    CK_M(dalloc(m, &m->q, T * qd));
+    CK_M(dalloc(m, &m->k, T * kvd));
+    CK_M(dalloc(m, &m->v, T * kvd));
+    CK_M(dalloc(m, &m->att, T * qd));
+    CK_M(dalloc(m, &m->hb, T * F));
+    CK_M(dalloc(m, &m->hb2, T * F));
+    CK_M(dalloc(m, &m->part, (size_t)PART_TOKSPLIT * c.n_head * (hd + 2)));
+    CK_M(dalloc(m, &m->logits, (size_t)m->max_seqs * c.vocab));
+    CK_M(cudaMemset(m->logits, 0, sizeof(float) * (size_t)m->max_seqs * c.vocab));
+    CK_M(dalloc(m, &m->d_tok, T));
+    CK_M(dalloc(m, &m->d_seq, T));
+    CK_M(dalloc(m, &m->d_pos, T));
+    CK_M(dalloc(m, &m->d_out, T));
+    CK_M(dalloc(m, &m->d_topk, T));
+    CK_M(dalloc(m, &m->d_temp, T));
+    CK_M(dalloc(m, &m->d_topp, T));
+    CK_M(dalloc(m, &m->d_seed, T));
+    CK_M(dalloc(m, &m->d_step, T));
+    m->nchunks = (c.vocab + 2047) / 2048;
+    CK_M(dalloc(m, &m->d_cand, (size_t)m->tdec * m->nchunks * 64));
+    CK_M(dalloc(m, &m->d_hist, (size_t)m->tdec * HIST_MAX));
+    CK_M(dalloc(m, &m->d_hist_col, 1));
+    CK_M(m->h_tok.alloc(T));
+    CK_M(m->h_seq.alloc(T));
+    CK_M(m->h_pos.alloc(T));
+    CK_M(m->h_out.alloc(T));
+    CK_M(m->h_topk.alloc(T));
+    CK_M(m->h_temp.alloc(T));
+    CK_M(m->h_topp.alloc(T));
+    CK_M(m->h_seed.alloc(T));
+    CK_M(m->h_step.alloc(T));
+    CK_M(m->h_hist.alloc((size_t)m->tdec * HIST_MAX));
+    for (int i = 0; i < 4; i++) CK_M(cudaEventCreate(&m->ev[i]));
+    rc = sync_check(m);
+    if (rc) return rc;
+    m->finalized = true;
+    return ACM_OK;
+}
+
+ACM_API int acm_model_destroy(acm_model *m) {
+    if (!m) return ACM_ERR_INVALID;
+    cudaSetDevice(m->e->device);
+    cudaStreamSynchronize(m->e->stream);
+    for (auto &g : m->graphs) cudaGraphExecDestroy(g.second.exec);
+    if (m->gemv_bench.exec) cudaGraphExecDestroy(m->gemv_bench.exec);
+    for (void *p : m->allocs) cudaFree(p);
+    m->h_page_table.release();
+    m->h_tok.release();
+    m->h_seq.release();
+    m->h_pos.release();
+    m->h_out.release();
+    m->h_topk.release();
+    m->h_temp.release();
+    m->h_topp.release();
+    m->h_seed.release();
+    m->h_step.release();
+    m->h_hist.release();
+    for (int i = 0; i < 4; i++)
+        if (m->ev[i]) cudaEventDestroy(m->ev[i]);
+    delete m;
+    return ACM_OK;
+}
+
+ACM_API const char *acm_last_error(acm_model *m) { return m ? m->err.c_str() : "null model"; }
+
+ACM_API int acm_model_config(acm_model *m, acm_config *out) {
+    if (!m || !out) return ACM_ERR_INVALID;
+    *out = m->c;
+    return ACM_OK;
+}
+
+ACM_API int acm_model_load_gguf(acm_engine *e, const char *path, int32_t max_ctx, int32_t max_seqs,
+                                acm_model **out) {
+    if (!e || !path || !out) return ACM_ERR_INVALID;
+    *out = nullptr;
+    const int fd = open(path, O_RDONLY);
+    if (fd < 0) return set_eerr(e, ACM_ERR_IO, fmt("open %s: %s", path, strerror(errno)));
+    struct stat sb;
+    if (fstat(fd, &sb) != 0 || sb.st_size <= 0) {
+        close(fd);
+        return set_eerr(e, ACM_ERR_IO, fmt("stat %s failed", path));
+    }
+    const size_t len = (size_t)sb.st_size;
+    // read-only private mapping as the reference's readModel (app/model_unix.go:15-34)
+    void *map = mmap(nullptr, len, PROT_READ, MAP_PRIVATE, fd, 0);
+    close(fd);
+    if (map == MAP_FAILED) return set_eerr(e, ACM_ERR_IO, fmt("mmap %s failed", path));
+    madvise(map, len, MADV_WILLNEED);
+    gguf::File f;
+    std::string err;
+    int rc = gguf::parse(static_cast<const uint8_t *>(map), len, f, err);
+    acm_config c;
+    if (!rc) rc = gguf::load_config(f, max_ctx, c, err);
+    if (rc) {
+        munmap(map, len);
+        return set_eerr(e, rc, err);
+    }
+    acm_model *m = nullptr;
+    rc = acm_model_create(e, &c, max_seqs, &m);
+    if (rc) {
+        munmap(map, len);
+        return rc;
+    }
+    for (const std::string &name : f.order) {
+        const gguf::Tensor &t = f.tensors[name];
+        const bool used = name == "token_embd.weight" || name == "output.weight" || name == "output_norm.weight" ||
+                          name.rfind("blk.", 0) == 0;
+        if (!used) continue;
+        rc = acm_model_add_tensor(m, name.c_str(), t.type, t.dims.data(), (int)t.dims.size(), t.data, t.nbytes);
+        if (rc) break;
+    }
+    munmap(map, len);
+    if (!rc) rc = acm_model_finalize(m);
+    if (rc) {
+        e->err = m->err;
+        acm_model_destroy(m);
+        return rc;
+    }
+    *out = m;
+    return ACM_OK;
+}
+
+ACM_API int acm_load_config(const char *path, int32_t max_ctx, acm_config *out, char *err, int32_t errlen) {
+    auto fail = [&](int rc, const std::string &msg) {
+        if (err && errlen > 0) snprintf(err, (size_t)errlen, "%s", msg.c_str());
+        return rc;
+    };
+    if (!path || !out) return fail(ACM_ERR_INVALID, "null argument");
+    const int fd = open(path, O_RDONLY);
+    if (fd < 0) return fail(ACM_ERR_IO, fmt("open %s: %s", path, strerror(errno)));
+    struct stat sb;
+    if (fstat(fd, &sb) != 0 || sb.st_size <= 0) {
+        close(fd);
+        return fail(ACM_ERR_IO, fmt("stat %s failed", path));
+    }
+    const size_t len = (size_t)sb.st_size;
+    void *map = mmap(nullptr, len, PROT_READ, MAP_PRIVATE, fd, 0);
+    close(fd);
+    if (map == MAP_FAILED) return fail(ACM_ERR_IO, fmt("mmap %s failed", path));
+    gguf::File f;
+    std::string e;
+    int rc = gguf::parse(static_cast<const uint8_t *>(map), len, f, e);
+    if (!rc) rc = gguf::load_config(f, max_ctx, *out, e);
+    munmap(map, len);
+    return rc ? fail(rc, e) : ACM_OK;
+}
+
+ACM_API int acm_seq_open(acm_model *m, int32_t *seq_out) {
+    if (!m || !seq_out || !m->finalized) return set_err(m, ACM_ERR_INVALID, "model not finalized");
+    for (int i = 0; i < m->max_seqs; i++)
+        if (!m->seqs[i].open) {
+            m->seqs[i].open = true;
+            m->seqs[i].pos = 0;
+            *seq_out = i;
+            return ACM_OK;
+        }
+    return set_err(m, ACM_ERR_NO_SEQ, "no free sequence slot");
+}
+
+ACM_API int acm_seq_close(acm_model *m, int32_t seq) {
+    int rc = check_seq(m, seq);
+    if (rc) return rc;
+    Seq &s = m->seqs[seq];
+    for (int pg : s.pages) m->free_pages.push_back(pg);
+    s.pages.clear();
+    s.open = false;
+    s.pos = 0;
+    return ACM_OK;
+}
+
+ACM_API int acm_seq_reset(acm_model *m, int32_t seq) {
+    int rc = check_seq(m, seq);
+    if (rc) return rc;
+    m->seqs[seq].pos = 0;  // Reset keeps the cache pages, model.go:458-460
+    return ACM_OK;
+}
+
+ACM_API int acm_seq_pos(acm_model *m, int32_t seq, int32_t *pos_out) {
+    int rc = check_seq(m, seq);
+    if (rc) return rc;
+    if (!pos_out) return ACM_ERR_INVALID;
+    *pos_out = m->seqs[seq].pos;
+    return ACM_OK;
+}
+
+ACM_API int acm_forward(acm_model *m, int32_t seq, const int32_t *toks, int32_t n, float *logits_out) {
+    int rc = check_seq(m, seq);
+    if (rc) return rc;
+    if (n <= 0 || !toks) return set_err(m, ACM_ERR_INVALID, "empty token batch");
+    cudaSetDevice(m->e->device);
+    Seq &s = m->seqs[seq];
+    if (s.pos + n > m->c.max_ctx)  // model.go:320-321
+        return set_err(m, ACM_ERR_CTX_EXCEEDED, fmt("context length exceeded (%d > %d)", s.pos + n, m->c.max_ctx));
+    const int64_t erows = m->embd->rows();
+    for (int i = 0; i < n; i++)
+        if (toks[i] < 0 || toks[i] >= erows) return set_err(m, ACM_ERR_INVALID, fmt("token id %d out of range", toks[i]));
+    CK_M(cudaEventRecord(m->ev[0], m->e->stream));
+    const int pos0 = s.pos;
+    rc = forward_seq(m, seq, toks, n);
+    if (rc) {
+        s.pos = pos0;
+        return rc;
+    }
+    CK_M(cudaEventRecord(m->ev[1], m->e->stream));
+    if (logits_out)
+        CK_M(cudaMemcpyAsync(logits_out, m->logits + (size_t)seq * m->c.vocab, sizeof(float) * m->c.vocab,
+                             cudaMemcpyDeviceToHost, m->e->stream));
+    if ((rc = sync_check(m))) return rc;
+    m->last_prefill_s = ev_seconds(m->ev[0], m->ev[1]);
+    return ACM_OK;
+}
+
+ACM_API int acm_sample(acm_model *m, int32_t seq, const acm_sampler *s, uint64_t step, int32_t *tok_out) {
+    int rc = check_seq(m, seq);
+    if (rc) return rc;
+    if (!tok_out) return ACM_ERR_INVALID;
+    cudaSetDevice(m->e->device);
+    m->h_seq.p[0] = seq;
+    fill_sampler(m, 0, s, step);
+    CK_M(cudaMemcpyAsync(m->d_seq, m->h_seq.p, sizeof(int32_t), cudaMemcpyHostToDevice, m->e->stream));
+    if ((rc = upload_sampler(m, 1))) return rc;
+    if ((rc = sample_pass(m, 1, !s || s->temp <= 0))) return rc;
+    CK_M(cudaMemcpyAsync(m->h_out.p, m->d_out, sizeof(int32_t), cudaMemcpyDeviceToHost, m->e->stream));
+    if ((rc = sync_check(m))) return rc;
+    *tok_out = m->h_out.p[0];
+    return ACM_OK;
+}
+
+ACM_API int acm_decode_step(acm_model *m, int32_t nseq, const int32_t *seqs, const int32_t *in_tok,
+                            const acm_sampler *samplers, const uint64_t *steps, int32_t *out_tok,
+                            float *logits_out) {
+    if (!m || !m->finalized) return set_err(m, ACM_ERR_INVALID, "model not finalized");
+    if (nseq <= 0 || nseq > m->tdec || !seqs || !in_tok || !out_tok)
+        return set_err(m, ACM_ERR_INVALID, "bad decode batch");
+    cudaSetDevice(m->e->device);
+    std::vector<char> seen(m->max_seqs, 0);
+    bool greedy = true;
+    const int64_t erows = m->embd->rows();
+    for (int i = 0; i < nseq; i++) {
+        int rc = check_seq(m, seqs[i]);
+        if (rc) return rc;
+        if (seen[seqs[i]]) return set_err(m, ACM_ERR_INVALID, "sequence repeated in a decode batch");
+        seen[seqs[i]] = 1;
+        const Seq &s = m->seqs[seqs[i]];
+        if (s.pos + 1 > m->c.max_ctx)
+            return set_err(m, ACM_ERR_CTX_EXCEEDED, fmt("context length exceeded (%d > %d)", s.pos + 1, m->c.max_ctx));
+        if (in_tok[i] < 0 || in_tok[i] >= erows) return set_err(m, ACM_ERR_INVALID, fmt("token id %d out of range", in_tok[i]));
+        if ((rc = ensure_pages(m, seqs[i], s.pos + 1))) return rc;
+        m->h_tok.p[i] = in_tok[i];
+        m->h_seq.p[i] = seqs[i];
+        m->h_pos.p[i] = s.pos;
+        fill_sampler(m, i, samplers ? &samplers[i] : nullptr, steps ? steps[i] : 0);
+        if (samplers && samplers[i].temp > 0) greedy = false;
+    }
+    int rc;
+    if ((rc = upload_meta(m, nseq))) return rc;
+    if ((rc = upload_sampler(m, nseq))) return rc;
+    CK_M(cudaMemsetAsync(m->d_hist_col, 0, sizeof(int32_t), m->e->stream));
+    CK_M(cudaEventRecord(m->ev[2], m->e->stream));
+    if ((rc = decode_graph_launch(m, nseq, greedy))) return rc;
+    CK_M(cudaEventRecord(m->ev[3], m->e->stream));
+    CK_M(cudaMemcpyAsync(m->h_out.p, m->d_out, sizeof(int32_t) * nseq, cudaMemcpyDeviceToHost, m->e->stream));
+    if ((rc = sync_check(m))) return rc;
+    m->last_decode_s = ev_seconds(m->ev[2], m->ev[3]);
+    for (int i = 0; i < nseq; i++) {
+        out_tok[i] = m->h_out.p[i];
+        m->seqs[seqs[i]].pos += 1;
+    }
+    if (logits_out)
+        for (int i = 0; i < nseq; i++)
+            CK_M(cudaMemcpy(logits_out + (size_t)i * m->c.vocab, m->logits + (size_t)seqs[i] * m->c.vocab,
+                            sizeof(float) * m->c.vocab, cudaMemcpyDeviceToHost));
+    return ACM_OK;
+}
+
+ACM_API int acm_generate(acm_model *m, int32_t seq, const int32_t *prompt, int32_t n_prompt, const acm_sampler *s,
+                         int32_t max_tok, int32_t stop_on_eos, int32_t *out_ids, int32_t *n_out, acm_stats *stats) {
+    int rc = check_seq(m, seq);
+    if (rc) return rc;
+    if (!n_out || (max_tok > 0 && !out_ids) || n_prompt < 0 || (n_prompt > 0 && !prompt))
+        return set_err(m, ACM_ERR_INVALID, "bad generate arguments");
+    cudaSetDevice(m->e->device);
+    *n_out = 0;
+    acm_stats st{0, 0, 0, 0};
+    Seq &sq = m->seqs[seq];
+    cudaStream_t stream = m->e->stream;
+    // sampler.go:116-121: chunk = min(1024, MaxCtx - pos)
+    const int chunk = std::min(TMAX, m->c.max_ctx - sq.pos);
+    if (chunk <= 0) return set_err(m, ACM_ERR_CTX_EXCEEDED, "context length exceeded");
+    const int64_t erows = m->embd->rows();
+    for (int i = 0; i < n_prompt; i++)
+        if (prompt[i] < 0 || prompt[i] >= erows) return set_err(m, ACM_ERR_INVALID, fmt("token id %d out of range", prompt[i]));
+    for (int i = 0; i < n_prompt; i += chunk) {
+        const int end = std::min(i + chunk, n_prompt);
+        if (sq.pos + (end - i) > m->c.max_ctx)
+            return set_err(m, ACM_ERR_CTX_EXCEEDED,
+                           fmt("context length exceeded (%d > %d)", sq.pos + end - i, m->c.max_ctx));
+        CK_M(cudaEventRecord(m->ev[0], stream));
+        if ((rc = forward_seq(m, seq, prompt + i, end - i))) return rc;
+        CK_M(cudaEventRecord(m->ev[1], stream));
+        if ((rc = sync_check(m))) return rc;
+        st.prefill_s += ev_seconds(m->ev[0], m->ev[1]);
+        st.prefill_toks += end - i;
+    }
+    m->last_prefill_s = st.prefill_s;
+    if (n_prompt == 0 || max_tok <= 0) {
+        if (stats) *stats = st;
+        return ACM_OK;
+    }
+    const bool greedy = !s || s->temp <= 0;
+    // id_0 from the prefill logits (step 0)
+    m->h_seq.p[0] = seq;
+    fill_sampler(m, 0, s, 0);
+    CK_M(cudaMemcpyAsync(m->d_seq, m->h_seq.p, sizeof(int32_t), cudaMemcpyHostToDevice, stream));
+    if ((rc = upload_sampler(m, 1))) return rc;
+    if ((rc = sample_pass(m, 1, greedy))) return rc;
+    CK_M(cudaMemcpyAsync(m->h_out.p, m->d_out, sizeof(int32_t), cudaMemcpyDeviceToHost, stream));
+    if ((rc = sync_check(m))) return rc;
+    // sampler.go:136-157: sample -> stop check -> append -> Forward.  The
+    // Forward+Sample pairs run on the device in chunks of up to HIST_MAX graph
+    // replays; step i of a chunk forwards the pending id and samples hist[i]
+    // with the draw of sample call n + 1 + i.
+    int n = 0;
+    int32_t id = m->h_out.p[0];
+    double dec = 0;
+    while (n < max_tok) {
+        if (stop_on_eos && (id == m->c.eos || id == m->c.eos2)) break;
+        const int room = m->c.max_ctx - sq.pos;
+        if (room <= 0) {
+            out_ids[n++] = id;
+            *n_out = n;
+            st.decode_s = dec;
+            if (stats) *stats = st;
+            return set_err(m, ACM_ERR_CTX_EXCEEDED, fmt("context length exceeded (%d > %d)", sq.pos + 1, m->c.max_ctx));
+        }
+        const int steps = std::min(std::min(HIST_MAX, max_tok - n), room);
+        if ((rc = ensure_pages(m, seq, sq.pos + steps))) return rc;
+        m->h_tok.p[0] = id;
+        m->h_seq.p[0] = seq;
+        m->h_pos.p[0] = sq.pos;
+        fill_sampler(m, 0, s, (uint64_t)n + 1);
+        if ((rc = upload_meta(m, 1))) return rc;
+        if ((rc = upload_sampler(m, 1))) return rc;
+        CK_M(cudaMemsetAsync(m->d_hist_col, 0, sizeof(int32_t), stream));
+        CK_M(cudaEventRecord(m->ev[2], stream));
+        for (int i = 0; i < steps; i++)
+            if ((rc = decode_graph_launch(m, 1, greedy))) return rc;
+        CK_M(cudaEventRecord(m->ev[3], stream));
+        CK_M(cudaMemcpyAsync(m->h_hist.p, m->d_hist, sizeof(int32_t) * steps, cudaMemcpyDeviceToHost, stream));
+        if ((rc = sync_check(m))) return rc;
+        dec += ev_seconds(m->ev[2], m->ev[3]);
+        for (int i = 0; i < steps; i++) {
+            out_ids[n++] = id;  // step i forwarded `id`
+            sq.pos += 1;
+            st.decode_toks++;
+            id = m->h_hist.p[i];
+            if (n >= max_tok) break;
+            if (stop_on_eos && (id == m->c.eos || id == m->c.eos2)) break;  // later steps are discarded
+        }
+    }
+    m->last_decode_s = dec;
+    st.decode_s = dec;
+    *n_out = n;
+    if (stats) *stats = st;
+    return ACM_OK;
+}
+
+ACM_API int32_t acm_max_logit(const float *logits, int32_t n) {
+    int32_t best = 0;
+    for (int32_t i = 1; i < n; i++)
+        if (logits[i] > logits[best]) best = i;
+    return best;
+}
+
+ACM_API int acm_model_last_timing(acm_model *m, double *prefill_s, double *decode_s) {
+    if (!m) return ACM_ERR_INVALID;
+    if (prefill_s) *prefill_s = m->last_prefill_s;
+    if (decode_s) *decode_s = m->last_decode_s;
+    return ACM_OK;
+}
+
+ACM_API uint64_t acm_kernel_launches(void) { return g_kernel_launches.load(); }
+
+ACM_API int acm_model_bench_gemv(acm_model *m, int32_t reps, double *sec_per_pass, double *bytes_per_pass,
+                                 int32_t *launches_per_pass) {
+    if (!m || !m->finalized || reps <= 0) return set_err(m, ACM_ERR_INVALID, "bad arguments");
+    cudaSetDevice(m->e->device);
+    const acm_config &c = m->c;
+    cudaStream_t st = m->e->stream;
+    const int E = c.n_embd, hd = c.head_dim, qd = c.n_head * hd, kvd = c.n_head_kv * hd, F = c.n_ff, S = m->e->num_sms;
+    const float eps = c.rms_eps;
+    double B = 0;
+    int nl = 0;
+    auto ops = [&]() -> int {
+        B = 0;
+        nl = 0;
+        for (int l = 0; l < c.n_layers; l++) {
+            const Layer &L = m->layers[l];
+            GemvSegDesc sg[3] = {{L.q->d, nullptr, (int)L.q->type, qd, EPI_STORE, m->q, qd, L.q_b, nullptr},
+                                 {L.k->d, nullptr, (int)L.k->type, kvd, EPI_STORE, m->k, kvd, L.k_b, nullptr},
+                                 {L.v->d, nullptr, (int)L.v->type, kvd, EPI_STORE, m->v, kvd, L.v_b, nullptr}};
+            CK_M(gemv_launch(sg, 3, m->x, E, E, 1, L.attn_nw, eps, S, st));
+            B += (double)(L.q->nbytes + L.k->nbytes + L.v->nbytes) + 4.0 * (2 * E + qd + 2 * kvd);
+            GemvSegDesc so{L.o->d, nullptr, (int)L.o->type, E, EPI_ADD, m->x, E, nullptr, nullptr};
+            CK_M(gemv_launch(&so, 1, m->att, qd, qd, 1, nullptr, eps, S, st));
+            B += (double)L.o->nbytes + 4.0 * (qd + 2 * E);
+            if (L.gate->type == L.up->type) {
+                GemvSegDesc sf{L.gate->d, L.up->d, (int)L.gate->type, F, EPI_SWIGLU, m->hb, F, nullptr, nullptr};
+                CK_M(gemv_launch(&sf, 1, m->x, E, E, 1, L.ffn_nw, eps, S, st));
+            } else {
+                GemvSegDesc sf[2] = {{L.gate->d, nullptr, (int)L.gate->type, F, EPI_STORE, m->hb, F, nullptr, nullptr},
+                                     {L.up->d, nullptr, (int)L.up->type, F, EPI_STORE, m->hb2, F, nullptr, nullptr}};
+                CK_M(gemv_launch(sf, 2, m->x, E, E, 1, L.ffn_nw, eps, S, st));
+            }
+            B += (double)(L.gate->nbytes + L.up->nbytes) + 4.0 * (2 * E + F);
+            GemvSegDesc sd{L.down->d, nullptr, (int)L.down->type, E, EPI_ADD, m->x, E, nullptr, nullptr};
+            CK_M(gemv_launch(&sd, 1, m->hb, F, F, 1, nullptr, eps, S, st));
+            B += (double)L.down->nbytes + 4.0 * (F + 2 * E);
+            nl += 4;
+        }
+        GemvSegDesc so{m->out->d, nullptr, (int)m->out->type, m->out->rows(), EPI_STORE, m->logits, c.vocab, nullptr,
+                       m->d_seq};
+        CK_M(gemv_launch(&so, 1, m->x, E, E, 1, m->out_nw, eps, S, st));
+        B += (double)m->out->nbytes + 4.0 * (2 * E + (double)m->out->rows());
+        nl += 1;
+        return ACM_OK;
+    };
+    m->h_seq.p[0] = 0;
+    CK_M(cudaMemcpyAsync(m->d_seq, m->h_seq.p, sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    int rc;
+    if (!m->gemv_bench.exec) {
+        if ((rc = ops())) return rc;  // warm-up (kernel attributes) outside capture
+        if ((rc = sync_check(m))) return rc;
+        const unsigned long long before = g_kernel_launches.load();
+        cudaGraph_t g = nullptr;
+        CK_M(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        rc = ops();
+        cudaError_t ce = cudaStreamEndCapture(st, &g);
+        const unsigned long long captured = g_kernel_launches.load() - before;
+        g_kernel_launches -= captured;
+        if (rc || ce != cudaSuccess) {
+            if (g) cudaGraphDestroy(g);
+            return rc ? rc : set_err(m, ACM_ERR_CUDA, "capture failed");
+        }
+        cudaError_t ie = cudaGraphInstantiate(&m->gemv_bench.exec, g, 0);
+        cudaGraphDestroy(g);
+        if (ie != cudaSuccess) return set_err(m, ACM_ERR_CUDA, "instantiate failed");
+        m->gemv_bench.kernels = captured;
+    } else {
+        // recompute byte/launch counts without launching: run ops under a
+        // throwaway capture
+        cudaGraph_t g = nullptr;
+        const unsigned long long before = g_kernel_launches.load();
+        CK_M(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        rc = ops();
+        cudaStreamEndCapture(st, &g);
+        g_kernel_launches -= g_kernel_launches.load() - before;
+        if (g) cudaGraphDestroy(g);
+        if (rc) return rc;
+    }
+    CK_M(cudaGraphLaunch(m->gemv_bench.exec, st));  // warm
+    CK_M(cudaEventRecord(m->ev[0], st));
+    for (int i = 0; i < reps; i++) CK_M(cudaGraphLaunch(m->gemv_bench.exec, st));
+    CK_M(cudaEventRecord(m->ev[1], st));
+    if ((rc = sync_check(m))) return rc;
+    g_kernel_launches += (unsigned long long)(reps + 1) * m->gemv_bench.kernels;
+    if (sec_per_pass) *sec_per_pass = ev_seconds(m->ev[0], m->ev[1]) / reps;
+    if (bytes_per_pass) *bytes_per_pass = B;
+    if (launches_per_pass) *launches_per_pass = nl;
+    return ACM_OK;
+}
+
+// ---- kernel-level entry points ----
+
+static int scratch(acm_engine *e, size_t bytes, uint8_t **p) {
+    if (e->scratch_bytes < bytes) {
+        if (e->scratch) cudaFree(e->scratch);
+        e->scratch = nullptr;
+        e->scratch_bytes = 0;
+        CK_E(cudaMalloc(&e->scratch, bytes));
+        e->scratch_bytes = bytes;
+    }
+    *p = static_cast<uint8_t *>(e->scratch);
+    return ACM_OK;
+}
+
+static size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
+
+ACM_API int acm_dequant(acm_engine *e, uint32_t ggml_type, const void *host_bytes, int64_t nrows, int64_t k,
+                        float *host_out) {
+    if (!e || !host_bytes || !host_out || nrows <= 0 || k <= 0) return ACM_ERR_INVALID;
+    if (!type_ok((int)ggml_type)) return set_eerr(e, ACM_ERR_UNSUPPORTED_TYPE, "unsupported type");
+    if (k % 32 || k % blk_elems((int)ggml_type)) return set_eerr(e, ACM_ERR_INVALID, "row length not a multiple of 32");
+    cudaSetDevice(e->device);
+    const size_t wb = (size_t)nrows * row_bytes((int)ggml_type, k), ob = sizeof(float) * nrows * k;
+    uint8_t *s = nullptr;
+    int rc = scratch(e, al256(wb + 64) + ob, &s);
+    if (rc) return rc;
+    float *o = reinterpret_cast<float *>(s + al256(wb + 64));
+    CK_E(cudaMemcpyAsync(s, host_bytes, wb, cudaMemcpyHostToDevice, e->stream));
+    CK_E(cudaMemsetAsync(s + wb, 0, 64, e->stream));
+    CK_E(dequant_launch((int)ggml_type, s, k, nrows, nullptr, nrows, o, k, e->stream));
+    CK_E(cudaMemcpyAsync(host_out, o, ob, cudaMemcpyDeviceToHost, e->stream));
+    CK_E(cudaStreamSynchronize(e->stream));
+    if (read_and_clear_dev_error()) return set_eerr(e, ACM_ERR_TIMEOUT, "device-side error flag set");
+    return ACM_OK;
+}
+
+ACM_API int acm_matmul_dev(acm_engine *e, uint32_t ggml_type, const void *d_w, int64_t n, int64_t k,
+                           const float *d_x, int32_t m, float *d_y) {
+    if (!e || !d_w || !d_x || !d_y || n <= 0 || k <= 0 || m <= 0) return ACM_ERR_INVALID;
+    if (!type_ok((int)ggml_type)) return set_eerr(e, ACM_ERR_UNSUPPORTED_TYPE, "unsupported type");
+    if (k % 32 || k % blk_elems((int)ggml_type)) return set_eerr(e, ACM_ERR_INVALID, "row length not a multiple of 32");
+    if (n > INT32_MAX) return set_eerr(e, ACM_ERR_INVALID, "too many rows");
+    if (gemv_supported((int)ggml_type, k, m)) {
+        GemvSegDesc sg{d_w, nullptr, (int)ggml_type, n, EPI_STORE, d_y, (int)n, nullptr, nullptr};
+        CK_E(gemv_launch(&sg, 1, d_x, (int)k, k, m, nullptr, 0.f, e->num_sms, e->stream));
+    } else {
+        CK_E(gemm_launch({d_w, nullptr, (int)ggml_type, n, k, m, d_x, (int)k, d_y, (int)n, EPI_STORE, nullptr, nullptr},
+                         e->stream));
+    }
+    return ACM_OK;
+}
+
+ACM_API int acm_matmul(acm_engine *e, uint32_t ggml_type, const void *host_w, int64_t n, int64_t k,
+                       const float *host_x, int32_t m, float *host_y) {
+    if (!e || !host_w || !host_x || !host_y || n <= 0 || k <= 0 || m <= 0) return ACM_ERR_INVALID;
+    if (!type_ok((int)ggml_type)) return set_eerr(e, ACM_ERR_UNSUPPORTED_TYPE, "unsupported type");
+    if (k % 32 || k % blk_elems((int)ggml_type)) return set_eerr(e, ACM_ERR_INVALID, "row length not a multiple of 32");
+    cudaSetDevice(e->device);
+    const size_t wb = (size_t)n * row_bytes((int)ggml_type, k), xb = sizeof(float) * m * k, yb = sizeof(float) * m * n;
+    uint8_t *s = nullptr;
+    int rc = scratch(e, al256(wb + 64) + al256(xb) + yb, &s);
+    if (rc) return rc;
+    float *dx = reinterpret_cast<float *>(s + al256(wb + 64));
+    float *dy = reinterpret_cast<float *>(s + al256(wb + 64) + al256(xb));
+    CK_E(cudaMemcpyAsync(s, host_w, wb, cudaMemcpyHostToDevice, e->stream));
+    CK_E(cudaMemsetAsync(s + wb, 0, 64, e->stream));
+    CK_E(cudaMemcpyAsync(dx, host_x, xb, cudaMemcpyHostToDevice, e->stream));
+    if ((rc = acm_matmul_dev(e, ggml_type, s, n, k, dx, m, dy))) return rc;
+    CK_E(cudaMemcpyAsync(host_y, dy, yb, cudaMemcpyDeviceToHost, e->stream));
+    CK_E(cudaStreamSynchronize(e->stream));
+    if (read_and_clear_dev_error()) return set_eerr(e, ACM_ERR_TIMEOUT, "a device-side wait timed out");
+    return ACM_OK;
+}
+
+ACM_API int acm_sample_logits(acm_engine *e, const float *host_logits, int32_t n, const acm_sampler *s,
+                              uint64_t step, int32_t *tok_out) {
+    if (!e || !host_logits || n <= 0 || !tok_out) return ACM_ERR_INVALID;
+    cudaSetDevice(e->device);
+    const int nchunks = (n + 2047) / 2048;
+    const size_t lb = al256(sizeof(float) * n), cb = al256(sizeof(uint64_t) * nchunks * 64);
+    uint8_t *p = nullptr;
+    int rc = scratch(e, lb + cb + 256 * 8, &p);
+    if (rc) return rc;
+    float *dl = reinterpret_cast<float *>(p);
+    uint64_t *cand = reinterpret_cast<uint64_t *>(p + lb);
+    uint8_t *par = p + lb + cb;
+    double *temp = reinterpret_cast<double *>(par);
+    double *topp = temp + 1;
+    uint64_t *seed = reinterpret_cast<uint64_t *>(par + 16), *stp = seed + 1;
+    int32_t *topk = reinterpret_cast<int32_t *>(par + 32), *out = topk + 1;
+    uint8_t hostpar[64] = {};
+    const double tv = s ? s->temp : 0.0, pv = s ? s->top_p : 0.0;
+    const uint64_t sv = s ? s->seed : 0;
+    const int32_t kv = s ? s->top_k : 0;
+    memcpy(hostpar, &tv, 8);
+    memcpy(hostpar + 8, &pv, 8);
+    memcpy(hostpar + 16, &sv, 8);
+    memcpy(hostpar + 24, &step, 8);
+    memcpy(hostpar + 32, &kv, 4);
+    CK_E(cudaMemcpyAsync(dl, host_logits, sizeof(float) * n, cudaMemcpyHostToDevice, e->stream));
+    CK_E(cudaMemcpyAsync(par, hostpar, 40, cudaMemcpyHostToDevice, e->stream));
+    SampleDesc sd{dl, nullptr, n, n, temp, topk, topp, seed, stp, out, cand, nchunks};
+    CK_E(sample_launch(sd, 1, !s || s->temp <= 0, e->stream));
+    int32_t res = -1;
+    CK_E(cudaMemcpyAsync(&res, out, sizeof(int32_t), cudaMemcpyDeviceToHost, e->stream));
+    CK_E(cudaStreamSynchronize(e->stream));
+    *tok_out = res;
+    return ACM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,192 @@
+// k_attn.cu -- GQA attention over the paged KV cache (model.go:384-408).
+//
+// One CTA handles one (token, kv-head) pair and a contiguous range of cache
+// positions; the G = n_head / n_head_kv query heads that share the kv head
+// are processed together so each K/V row is read once for all of them.
+//   phase 1: warp w scores positions w, w+4, ... (lane-split dot product,
+//            shuffle reduction), times 1/sqrt(head_dim) as the reference;
+//   phase 2: per head, max, fastExp(s - max), sum (softmax, model.go:297-313);
+//   phase 3: out[d] = sum_p p_p * v_p[d], positions in increasing order
+//            (axpy loop, model.go:404-406).
+// Decode batches are small, so the position range of a token is split over
+// `nsplit` CTAs (flash-decoding); a second kernel merges the partial
+// (sum e*v, max, sum e) triples.
+#include <float.h>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "quant.cuh"
+
+namespace acm {
+
+__device__ __forceinline__ const float *kv_row(const float *pool, const KVDesc &kv, int layer, int seq, int pos) {
+    const int page = kv.page_table[(int64_t)seq * kv.max_pages + (pos / kv.page_size)];
+    return pool + (int64_t)layer * kv.layer_stride + ((int64_t)page * kv.page_size + (pos % kv.page_size)) * kv.kvd;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) k_attn(const AttnDesc a, const KVDesc kv, int layer, TokMeta tm,
+                                              int chunk_max) {
+    extern __shared__ float sm[];
+    constexpr int PER = HD / 32;  // q/k elements per lane
+    const int t = blockIdx.x, g = blockIdx.y, split = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = a.n_head / a.n_head_kv;
+    const int nh = a.n_head, qd = nh * HD;
+    const int seq = tm.seq[t], pos = tm.pos[t];
+    const int L = pos + 1;
+    int lo = 0, hi = L;
+    if (a.nsplit > 1) {
+        const int chunk = (L + a.nsplit - 1) / a.nsplit;
+        lo = min(L, split * chunk);
+        hi = min(L, lo + chunk);
+    }
+    const int n = hi - lo;
+    float *qs = sm;                    // [G][HD]
+    float *sc = sm + G * HD;           // [G][chunk_max]
+    float *stat = sc + G * chunk_max;  // [G][2] (max, sum)
+    float *red = stat + 2 * G;         // [(128/HD - 1)][G][HD] position-group partials
+    if (n <= 0) {
+        // empty split: neutral partial
+        if (threadIdx.x < G) {
+            float *pp = a.part + (((int64_t)t * nh + g * G + threadIdx.x) * a.nsplit + split) * (HD + 2);
+            pp[HD] = -FLT_MAX;
+            pp[HD + 1] = 0.f;
+        }
+        for (int i = threadIdx.x; i < G * HD; i += 128) {
+            const int hh = i / HD, d = i - hh * HD;
+            a.part[(((int64_t)t * nh + g * G + hh) * a.nsplit + split) * (HD + 2) + d] = 0.f;
+        }
+        return;
+    }
+    for (int i = threadIdx.x; i < G * HD; i += 128) qs[i] = a.q[(int64_t)t * qd + (int64_t)g * G * HD + i];
+    __syncthreads();
+    // phase 1: scores
+    for (int p = lo + warp; p < hi; p += 4) {
+        const float *kr = kv_row(kv.k, kv, layer, seq, p) + g * HD;
+        float kk[PER];
+#pragma unroll
+        for (int e = 0; e < PER; e++) kk[e] = kr[lane + 32 * e];
+        for (int h = 0; h < G; h++) {
+            float s = 0.f;
+#pragma unroll
+            for (int e = 0; e < PER; e++) s = fmaf(qs[h * HD + lane + 32 * e], kk[e], s);
+            s = warp_sum(s);
+            if (lane == 0) sc[h * chunk_max + (p - lo)] = __fmul_rn(s, a.scale);
+        }
+    }
+    __syncthreads();
+    // phase 2: softmax per head (warp h handles heads h, h+4, ...)
+    for (int h = warp; h < G; h += 4) {
+        float *s = sc + h * chunk_max;
+        float mx = -FLT_MAX;
+        for (int i = lane; i < n; i += 32) mx = fmaxf(mx, s[i]);
+        mx = warp_max(mx);
+        float sum = 0.f;
+        for (int i = lane; i < n; i += 32) {
+            const float e = fast_exp(__fsub_rn(s[i], mx));
+            s[i] = e;
+            sum += e;
+        }
+        sum = warp_sum(sum);
+        if (a.nsplit == 1) {
+            for (int i = lane; i < n; i += 32) s[i] = __fdiv_rn(s[i], sum);
+        }
+        if (lane == 0) {
+            stat[2 * h] = mx;
+            stat[2 * h + 1] = sum;
+        }
+    }
+    __syncthreads();
+    // phase 3: P.V ; 128 threads cover HD dims x (128/HD) position groups
+    constexpr int GROUPS = 128 / HD;
+    const int d = threadIdx.x % HD, grp = threadIdx.x / HD;
+    float acc[8];
+#pragma unroll
+    for (int h = 0; h < 8; h++) acc[h] = 0.f;
+    for (int p = lo + grp; p < hi; p += GROUPS) {
+        const float v = kv_row(kv.v, kv, layer, seq, p)[g * HD + d];
+#pragma unroll
+        for (int h = 0; h < 8; h++)
+            if (h < G) acc[h] = fmaf(sc[h * chunk_max + (p - lo)], v, acc[h]);
+    }
+    if (GROUPS > 1) {
+        if (grp > 0)
+            for (int h = 0; h < G; h++) red[((grp - 1) * G + h) * HD + d] = acc[h];
+        __syncthreads();
+        if (grp == 0)
+            for (int gg = 1; gg < GROUPS; gg++)
+                for (int h = 0; h < G; h++) acc[h] += red[((gg - 1) * G + h) * HD + d];
+    }
+    if (grp != 0) return;
+    if (a.nsplit == 1) {
+        for (int h = 0; h < G; h++) a.out[(int64_t)t * qd + (int64_t)(g * G + h) * HD + d] = acc[h];
+    } else {
+        for (int h = 0; h < G; h++) {
+            float *pp = a.part + (((int64_t)t * nh + g * G + h) * a.nsplit + split) * (HD + 2);
+            pp[d] = acc[h];
+            if (d == 0) {
+                pp[HD] = stat[2 * h];
+                pp[HD + 1] = stat[2 * h + 1];
+            }
+        }
+    }
+}
+
+// Merge split partials: out = sum_s w_s * o_s / sum_s w_s * l_s with
+// w_s = fastExp(m_s - max_s m_s).
+template <int HD>
+__global__ void k_attn_combine(const AttnDesc a) {
+    const int t = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+    const float *pp = a.part + ((int64_t)t * a.n_head + h) * a.nsplit * (HD + 2);
+    float mx = -FLT_MAX;
+    for (int s = 0; s < a.nsplit; s++)
+        if (pp[s * (HD + 2) + HD + 1] > 0.f) mx = fmaxf(mx, pp[s * (HD + 2) + HD]);
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < a.nsplit; s++) {
+        const float l = pp[s * (HD + 2) + HD + 1];
+        if (l > 0.f) {
+            const float w = fast_exp(pp[s * (HD + 2) + HD] - mx);
+            num = fmaf(w, pp[s * (HD + 2) + d], num);
+            den = fmaf(w, l, den);
+        }
+    }
+    a.out[(int64_t)t * a.n_head * HD + (int64_t)h * HD + d] = num / den;
+}
+
+cudaError_t attention_launch(const AttnDesc &a, const KVDesc &kv, int layer, TokMeta tm, int ntok, int max_pos,
+                             cudaStream_t st) {
+    if (ntok <= 0) return cudaSuccess;
+    const int G = a.n_head / a.n_head_kv;
+    if (G > 8 || a.n_head % a.n_head_kv) return cudaErrorInvalidValue;
+    const int L = max_pos + 1;
+    const int chunk_max = (L + a.nsplit - 1) / a.nsplit;
+    const int HD = a.head_dim;
+    const size_t red = (size_t)(128 / HD > 1 ? (128 / HD - 1) : 0) * G * HD;
+    const size_t smem = ((size_t)G * HD + (size_t)G * chunk_max + 2 * G + red) * sizeof(float);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    dim3 grid(ntok, a.n_head_kv, a.nsplit);
+    static bool attr[64][2] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (HD == 128) {
+        if (!attr[dev & 63][0]) {
+            cudaFuncSetAttribute(k_attn<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            attr[dev & 63][0] = true;
+        }
+        k_attn<128><<<grid, 128, smem, st>>>(a, kv, layer, tm, chunk_max);
+        if (a.nsplit > 1) k_attn_combine<128><<<dim3(ntok, a.n_head), 128, 0, st>>>(a);
+    } else if (HD == 64) {
+        if (!attr[dev & 63][1]) {
+            cudaFuncSetAttribute(k_attn<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            attr[dev & 63][1] = true;
+        }
+        k_attn<64><<<grid, 128, smem, st>>>(a, kv, layer, tm, chunk_max);
+        if (a.nsplit > 1) k_attn_combine<64><<<dim3(ntok, a.n_head), 64, 0, st>>>(a);
+    } else {
+        return cudaErrorInvalidValue;
+    }
+    return launched(a.nsplit > 1 ? 2 : 1);
+}
+
+}  // namespace acm

@@ -1,0 +1,170 @@
+// kernels.h -- launch interfaces of the engine's CUDA kernels (host side).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+
+namespace acm {
+
+// Device error flag values (set by kernels, read by the host after a sync).
+enum : int { DEV_ERR_NONE = 0, DEV_ERR_TIMEOUT = 1, DEV_ERR_BOUNDS = 2 };
+
+// Epilogues shared by the GEMV and GEMM kernels.
+enum : int {
+    EPI_STORE = 0,   // y = W x (+ bias)
+    EPI_ADD = 1,     // y += W x          (residual update, model.go:411-413, :424-426)
+    EPI_SWIGLU = 2,  // y = silu(Wg x) * (Wu x)   (model.go:420-422)
+};
+
+// One weight matrix (or gate/up pair) of a multi-segment GEMV launch.
+struct GemvSeg {
+    const uint8_t *w, *w2;  // tensor bytes (w2: up-projection of a SwiGLU pair)
+    int64_t rb, rb2;        // row bytes
+    int type;               // ggml type (w2 has the same type)
+    int n;                  // rows
+    int cta0, ncta;         // this segment's CTA range
+    int rows_per_stage;
+    int epi;
+    float *y;               // output [m][ldy]
+    int ldy;
+    const float *bias;      // optional, n floats
+    const int32_t *yrow;    // optional: output row of token m (default m)
+};
+
+constexpr int GEMV_MAX_SEG = 4;
+constexpr int GEMV_THREADS = 288;  // 8 consumer warps + 1 producer warp
+constexpr int GEMV_NS_MAX = 8;
+
+struct GemvArgs {
+    GemvSeg seg[GEMV_MAX_SEG];
+    int nseg;
+    const float *x;      // activations [m][ldx] (fp32)
+    int ldx;
+    int k;
+    int m;
+    const float *norm_w; // optional RMSNorm weight applied to x in the prologue
+    float eps;
+    int ns;              // pipeline stages
+    int stage_bytes;
+    int stage_off;       // byte offset of the stage ring in shared memory
+};
+
+// Plans CTA ranges / stages and launches.  Returns a cudaError_t.
+struct GemvSegDesc {
+    const void *w, *w2;
+    int type;
+    int64_t n;
+    int epi;
+    float *y;
+    int ldy;
+    const float *bias;
+    const int32_t *yrow;
+};
+cudaError_t gemv_launch(const GemvSegDesc *segs, int nseg, const float *x, int ldx, int64_t k, int m,
+                        const float *norm_w, float eps, int num_sms, cudaStream_t st);
+bool gemv_supported(int type, int64_t k, int m);
+
+// Prefill / batched GEMM: y[m][n] (epi) x[m][k] . W[n][k]^T.
+struct GemmDesc {
+    const void *w, *w2;
+    int type;
+    int64_t n, k;
+    int m;
+    const float *x;
+    int ldx;
+    float *y;
+    int ldy;
+    int epi;
+    const float *bias;
+    const int32_t *yrow;    // optional: output row of token m (default m)
+};
+cudaError_t gemm_launch(const GemmDesc &d, cudaStream_t st);
+
+// Dequantize rows (exact): rows either consecutive (row_ids == nullptr) or
+// gathered by id (embedding lookup, model.go:338-340).
+cudaError_t dequant_launch(int type, const void *w, int64_t k, int64_t nrows, const int32_t *row_ids,
+                           int64_t src_rows, float *out, int64_t ldo, cudaStream_t st);
+
+// RMSNorm of m rows (model.go:213-222): y = x * scale * w.
+cudaError_t rmsnorm_launch(const float *x, int ldx, const float *w, float *y, int ldy, int m, int n, float eps,
+                           cudaStream_t st);
+
+// Per-token metadata of a token batch.
+struct TokMeta {
+    const int32_t *seq;   // sequence slot of each token
+    const int32_t *pos;   // position of each token
+};
+
+// Paged KV cache geometry.
+struct KVDesc {
+    float *k, *v;               // pools [layer][page][page_size][kvd]
+    const int32_t *page_table;  // [max_seqs][max_pages]
+    int max_pages;
+    int page_size;              // positions per page (power of two)
+    int64_t layer_stride;       // floats per layer in each pool
+    int kvd;
+};
+
+// QK-norm + RoPE on q (in place) and k, then append k, v to the cache
+// (model.go:362-382).
+struct RopeDesc {
+    float *q;          // [ntok][qd]
+    const float *k, *v;// [ntok][kvd]
+    const float *q_nw, *k_nw;  // optional per-head RMSNorm weights
+    const float2 *tab; // [max_ctx][rope_dim/2] (cos, sin)
+    int n_head, n_head_kv, head_dim, rope_dim, interleaved;
+    float eps;
+};
+cudaError_t rope_append_launch(const RopeDesc &r, const KVDesc &kv, int layer, TokMeta tm, int ntok,
+                               cudaStream_t st);
+
+// Attention over the paged cache (model.go:384-408).
+struct AttnDesc {
+    const float *q;   // [ntok][qd]
+    float *out;       // [ntok][qd]
+    int n_head, n_head_kv, head_dim;
+    float scale;
+    float *part;      // split partials [ntok][n_head][nsplit][head_dim + 2]
+    int nsplit;
+};
+cudaError_t attention_launch(const AttnDesc &a, const KVDesc &kv, int layer, TokMeta tm, int ntok, int max_pos,
+                             cudaStream_t st);
+
+// y = silu(g) * u elementwise (fallback when gate and up differ in type).
+cudaError_t swiglu_launch(const float *g, const float *u, float *y, int64_t n, cudaStream_t st);
+
+// Sampler (sampler.go:19-98) over logits rows.
+struct SampleDesc {
+    const float *logits;
+    const int32_t *rows;     // logits row of token t (default t)
+    int64_t ld;
+    int vocab;
+    const double *temp;      // per token
+    const int32_t *top_k;
+    const double *top_p;
+    const uint64_t *seed;
+    const uint64_t *step;
+    int32_t *out;            // sampled ids [ntok]
+    uint64_t *cand;          // scratch [ntok][nchunks][64]
+    int nchunks;
+};
+cudaError_t sample_launch(const SampleDesc &s, int ntok, bool all_greedy, cudaStream_t st);
+
+// After a decode step: next input = sampled id, position + 1, step + 1, and
+// the id recorded in hist[t][hist_col] (device-side token loop).
+cudaError_t advance_launch(int32_t *tok, int32_t *pos, uint64_t *step, const int32_t *out, int32_t *hist,
+                           int hist_ld, int32_t *hist_col, int ntok, cudaStream_t st);
+
+// Device error flag (timeouts in bounded waits).
+int read_and_clear_dev_error();
+
+// Count of kernels this library has launched (graph replays add the kernels
+// the graph holds); every launcher returns through launched().
+extern std::atomic<unsigned long long> g_kernel_launches;
+inline cudaError_t launched(int n) {
+    g_kernel_launches += (unsigned long long)n;
+    return cudaGetLastError();
+}
+
+}  // namespace acm

@@ -1,0 +1,276 @@
+#!/usr/bin/env python
+"""Token-loop benchmark: decode & prefill tok/s of a Qwen3-0.6B-shape Q4_K_M
+model (28 layers, hidden 1024, 16/8 heads, head_dim 128, FFN 3072, vocab
+151936, Q4_K with Q6_K attn_v/ffn_down, random-init N(0, 0.02) weights),
+389-token seeded prompt, 64 greedy decode tokens, ctx 2048, batch 1 -- the
+workload the reference's README quotes (200 / 21 tok/s on a 12-core CPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one full Generate (prefill + 64 decode tokens, EOS stopping off so
+every step decodes exactly 64 tokens).  Multi-GPU: one process per GPU
+(torchrun), each rank serves its own independent sequence (weak scaling, no
+collective on the data path; a gloo group carries only the barrier and the
+max-over-ranks timing).
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+PROMPT_LEN, GEN_TOKENS, CTX = 389, 64, 2048
+METRIC = "decode & prefill tok/s, Qwen3-0.6B-shape Q4_K_M, 1/2/4/8 B200; % HBM roofline"
+WORKLOAD = "qwen3-0.6b-shape Q4_K_M (Q4_K + Q6_K attn_v/ffn_down), prompt 389, 64 greedy tokens, ctx 2048, batch 1"
+MODEL_DIR = os.environ.get("ACM_BENCH_DIR", os.path.join(tempfile.gettempdir(), "acm_bench"))
+
+
+def dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as td
+        td.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as td
+        td.barrier()
+
+
+def allreduce(vals, world, op="max"):
+    if world == 1:
+        return list(vals)
+    import torch
+    import torch.distributed as td
+    t = torch.tensor(vals, dtype=torch.float64)
+    td.all_reduce(t, op=td.ReduceOp.MAX if op == "max" else td.ReduceOp.SUM)
+    return t.tolist()
+
+
+def model_path(rank, world):
+    synth = importlib.import_module("auto-commit-msg_b200.synth")
+    path = os.path.join(MODEL_DIR, "qwen3-0.6b-q4km-seed0.gguf")
+    if rank == 0 and not os.path.exists(path):
+        os.makedirs(MODEL_DIR, exist_ok=True)
+        tmp = path + f".tmp{os.getpid()}"
+        synth.build_model(synth.qwen3_06b(), tmp, seed=0)
+        os.replace(tmp, path)
+    barrier(world)
+    return path, synth.prompt_ids(PROMPT_LEN, 151936, seed=1)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(gpu), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.flush()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.count(",") >= 8]
+        os.unlink(self.f.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if "Active" in v and "Not" not in v})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_baseline(path, prompt, nthreads=0, decode_tokens=8):
+    """The oracle (a C restatement of the reference's AVX2 CPU path) on the
+    host cores: prefill of the 389-token prompt + `decode_tokens` greedy steps."""
+    import oracle as O
+    O.set_threads(nthreads)
+    m = O.Model(path, CTX)
+    r = m.generate(prompt, max_tok=decode_tokens, stop_on_eos=False)
+    st = r["stats"]
+    m.close()
+    return {"decode_tok_s": st["decode_toks"] / st["decode_s"], "prefill_tok_s": st["prefill_toks"] / st["prefill_s"],
+            "cores": O.threads(), "seconds": st["decode_s"] + st["prefill_s"]}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    path, prompt = model_path(0, 1)
+    import oracle as O
+    O.set_threads(0)
+    m = O.Model(path, CTX)
+    dec_tok, dec_s, pre_tok, pre_s = 0, 0.0, 0, 0.0
+    for i in range(args.warmup + args.steps):
+        m.reset()
+        r = m.generate(prompt, max_tok=8, stop_on_eos=False)
+        if i >= args.warmup:
+            dec_tok += r["stats"]["decode_toks"]
+            dec_s += r["stats"]["decode_s"]
+            pre_tok += r["stats"]["prefill_toks"]
+            pre_s += r["stats"]["prefill_s"]
+    v = dec_tok / dec_s
+    sample = f"per step: prefill {PROMPT_LEN} tokens + 8 greedy decode tokens (of the 64-token workload)"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * (dec_s + pre_s) / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "prefill_tok_s": round(pre_tok / pre_s, 3),
+        "config": {"workload": WORKLOAD, "impl": "CPU restatement of the reference's AVX2 path (oracle/)"},
+        "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": O.threads(), "kind": "port", "sample": sample},
+        "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_ours(args, rank, world, local):
+    import torch
+    acm = importlib.import_module("auto-commit-msg_b200")
+    path, prompt = model_path(rank, world)
+    torch.cuda.set_device(local)
+    eng = acm.Engine(local)
+    m = acm.Load(path, CTX, engine=eng)
+    greedy = acm.Sampler(0.0)
+    for _ in range(args.warmup):
+        m.Generate(prompt, greedy, GEN_TOKENS, stop_on_eos=False)
+        m.Reset()
+    stream = torch.cuda.ExternalStream(eng.stream(), device=local)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    eng.sync()
+    clocks = Clocks(local)
+    n0 = acm.lib().acm_kernel_launches()
+    w0 = time.perf_counter()
+    ev0.record(stream)
+    dec_s = pre_s = 0.0
+    first = None
+    for _ in range(args.steps):
+        ids = m.Generate(prompt, greedy, GEN_TOKENS, stop_on_eos=False)
+        first = first or ids
+        dec_s += m.Stats.Decode
+        pre_s += m.Stats.Prefill
+        m.Reset()
+    ev1.record(stream)
+    eng.sync()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - w0
+    launches = acm.lib().acm_kernel_launches() - n0
+    barrier(world)
+    ck = clocks.stop()
+    dev = ev0.elapsed_time(ev1) * 1e-3
+    mx = allreduce([dec_s, pre_s, dev, wall], world, "max")
+    tot_launches = int(allreduce([float(launches)], world, "sum")[0])
+    dec_max, pre_max, dev_max, wall_max = mx
+    value = world * args.steps * GEN_TOKENS / dec_max
+    # dominant kernel: the fused dequant-GEMV launches of one decode token
+    sec, nbytes, nl = bench_gemv(acm, m)
+    peak, peak_kind = peaks()
+    achieved = nbytes / sec / 1e9
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            traffic = json.load(f).get("k_gemv_decode_pass_bytes")
+    except Exception:
+        pass
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(1e3 * dev_max / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (random-init weights, seeded prompt)",
+        "prefill_tok_s": round(world * args.steps * PROMPT_LEN / pre_max, 1),
+        "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": PROMPT_LEN + GEN_TOKENS,
+                   "parallelism": f"dp{world} (independent sequences)",
+                   "value": "decode tok/s (64 tokens per step / device time of the decode Forward calls)",
+                   "l2": "no flush: every decode token streams 366 MB of weights, > 126 MB L2"},
+        "e2e": {"value": round(world * args.steps * GEN_TOKENS / wall_max, 2), "unit": "tok/s",
+                "h2d_bytes_per_step": PROMPT_LEN * 4 + 128, "d2h_bytes_per_step": GEN_TOKENS * 4,
+                "note": "acm_generate through the C ABI: host prompt in, host ids out, prefill included"},
+        "roofline": {"bound": "hbm", "kernel": "k_gemv (all GEMV launches of one decode token)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "bytes_per_pass": int(nbytes), "launches_per_pass": nl, "traffic": traffic},
+        "gpu_launches": tot_launches,
+        "clocks": ck,
+    }
+    if world == 1 and rank == 0 and not args.no_cpu:
+        cb = cpu_baseline(path, prompt)
+        line["cpu_baseline"] = {"value": round(cb["decode_tok_s"], 3), "unit": "tok/s", "cores": cb["cores"],
+                                "kind": "port", "prefill_tok_s": round(cb["prefill_tok_s"], 2),
+                                "sample": f"prefill {PROMPT_LEN} tokens + 8 greedy decode tokens, oracle/ on all host threads"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    m.close()
+    eng.close()
+
+
+def bench_gemv(acm, m, reps=20):
+    import ctypes as C
+    sec, b, nl = C.c_double(), C.c_double(), C.c_int32()
+    rc = acm.lib().acm_model_bench_gemv(m.handle, reps, C.byref(sec), C.byref(b), C.byref(nl))
+    if rc:
+        raise RuntimeError(acm.lib().acm_last_error(m.handle).decode())
+    return sec.value, b.value, nl.value
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    rank, world, local = dist()
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as td
+            td.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

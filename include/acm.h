@@ -1,0 +1,207 @@
+/*
+ * acm.h -- C ABI of libacmcuda.so, the B200 engine for auto-commit-msg's
+ * token loop (load GGUF -> prefill -> decode with the top-k sampler).
+ *
+ * These are the entry points a cgo shim behind a `cuda` build tag in
+ * internal/infer binds.  Each declaration names the reference interface it
+ * replaces (paths are inside the auto-commit-msg tree).
+ *
+ * Conventions
+ *  - Every call returns an int status (ACM_OK = 0).  On failure the message is
+ *    available from acm_last_error(); the process is never aborted.
+ *  - Host pointers are borrowed for the duration of the call only.
+ *  - The library owns all device memory (weights, paged KV cache, activations,
+ *    logits).  A model is driven by one host thread at a time; separate models
+ *    (e.g. one per GPU) may be driven concurrently from separate threads.
+ */
+#ifndef ACM_H
+#define ACM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ACM_API __attribute__((visibility("default")))
+
+enum acm_status {
+    ACM_OK = 0,
+    ACM_ERR_INVALID = 1,          /* bad argument / state */
+    ACM_ERR_CTX_EXCEEDED = 2,     /* model.go:320-321 "context length exceeded" */
+    ACM_ERR_UNSUPPORTED_ARCH = 3, /* model.go:95 */
+    ACM_ERR_UNSUPPORTED_TYPE = 4, /* gguf.go:164, tensor.go:79 */
+    ACM_ERR_MISSING_TENSOR = 5,   /* model.go:136, :165, :198 */
+    ACM_ERR_OOM = 6,
+    ACM_ERR_CUDA = 7,
+    ACM_ERR_TIMEOUT = 8,
+    ACM_ERR_NO_SEQ = 9,
+    ACM_ERR_IO = 10,
+    ACM_ERR_FORMAT = 11            /* gguf.go:123-170 parse errors */
+};
+
+/* ggml tensor types accepted (gguf.go:31-40). */
+enum acm_ggml_type {
+    ACM_F32 = 0, ACM_F16 = 1, ACM_Q4_0 = 2, ACM_Q5_0 = 6, ACM_Q8_0 = 8,
+    ACM_Q4_K = 12, ACM_Q5_K = 13, ACM_Q6_K = 14
+};
+
+enum acm_arch { ACM_ARCH_QWEN3 = 0, ACM_ARCH_QWEN2 = 1, ACM_ARCH_LLAMA = 2 };
+enum acm_rope_scaling { ACM_ROPE_NONE = 0, ACM_ROPE_LINEAR = 1, ACM_ROPE_LLAMA3 = 2 };
+
+/* Model hyper-parameters: infer.Config, internal/infer/model.go:14-40. */
+typedef struct acm_config {
+    int32_t arch;
+    int32_t n_layers, n_embd, n_head, n_head_kv, head_dim, n_ff, vocab, max_ctx, rope_dim;
+    float rope_base;
+    int32_t rope_interleaved;
+    int32_t rope_scaling;
+    float rope_factor, rope_lo_f, rope_hi_f, rope_orig_ctx;
+    float rms_eps;
+    int32_t bos, eos, eos2;
+} acm_config;
+
+/* infer.Sampler (sampler.go:12-17).  The reference draws from a time-seeded
+ * PCG (internal/app/rand.go:10-13); here the uniform draw of decode step
+ * `step` is Philox4x32-10 keyed by `seed`, so runs are reproducible. */
+typedef struct acm_sampler {
+    double temp;   /* <= 0: greedy */
+    int32_t top_k; /* 0: 64 candidates */
+    double top_p;  /* only applied when 0 < top_p < 1 */
+    uint64_t seed;
+} acm_sampler;
+
+/* infer.Stats (sampler.go:101-106); durations in seconds. */
+typedef struct acm_stats {
+    int64_t prefill_toks;
+    double prefill_s;
+    int64_t decode_toks;
+    double decode_s;
+} acm_stats;
+
+typedef struct acm_engine acm_engine; /* one CUDA device + stream */
+typedef struct acm_model acm_model;   /* weights + paged KV + sequence slots */
+
+/* Library version string. */
+ACM_API const char *acm_version(void);
+
+/* Open a device.  No reference counterpart (the reference is CPU-only). */
+ACM_API int acm_open(int device, acm_engine **out);
+ACM_API int acm_close(acm_engine *e);
+ACM_API const char *acm_engine_error(acm_engine *e);
+
+/* Create an empty model for `cfg`; replaces infer.Load's allocation part
+ * (model.go:90-203).  max_seqs concurrent sequence slots, each up to
+ * cfg->max_ctx positions. */
+ACM_API int acm_model_create(acm_engine *e, const acm_config *cfg, int32_t max_seqs, acm_model **out);
+
+/* Copy one GGUF tensor's bytes UNCHANGED to HBM (the blocks stay in ggml
+ * layout; the model never holds a dequantized copy).  dims[0] is the
+ * innermost dimension as in gguf.Tensor.Dims (gguf.go:42-49).  host_bytes may
+ * point into an mmap and is not retained. */
+ACM_API int acm_model_add_tensor(acm_model *m, const char *name, uint32_t ggml_type, const uint64_t *dims,
+                                 int32_t ndims, const void *host_bytes, size_t nbytes);
+
+/* Bind tensors to layers and build the RoPE tables; the tensor checks of
+ * infer.Load (model.go:161-201) with the same error texts. */
+ACM_API int acm_model_finalize(acm_model *m);
+ACM_API int acm_model_destroy(acm_model *m);
+ACM_API const char *acm_last_error(acm_model *m);
+ACM_API int acm_model_config(acm_model *m, acm_config *out);
+
+/* Load a GGUF file (mmap, gguf.Parse gguf.go:121-174 and infer.Load
+ * model.go:90-203) and upload it: the host path a C or Python caller uses.
+ * max_ctx <= 0 or above the file's context_length selects the file's value. */
+ACM_API int acm_model_load_gguf(acm_engine *e, const char *path, int32_t max_ctx, int32_t max_seqs,
+                                acm_model **out);
+
+/* Parse a GGUF file and derive its configuration without touching a device:
+ * gguf.Parse (gguf.go:121-174) plus the metadata rules of infer.Load
+ * (model.go:91-151).  err receives a message on failure. */
+ACM_API int acm_load_config(const char *path, int32_t max_ctx, acm_config *out, char *err, int32_t errlen);
+
+/* Sequence slots.  A slot is one infer.Model's sequence state (pos + KV). */
+ACM_API int acm_seq_open(acm_model *m, int32_t *seq_out);
+ACM_API int acm_seq_close(acm_model *m, int32_t seq);
+/* Model.Reset, model.go:458-460: rewind to position 0 (KV pages are kept). */
+ACM_API int acm_seq_reset(acm_model *m, int32_t seq);
+/* Model.Pos, model.go:455-456. */
+ACM_API int acm_seq_pos(acm_model *m, int32_t seq, int32_t *pos_out);
+
+/* Model.Forward, model.go:315-442: evaluate n tokens at consecutive positions
+ * of `seq`; the last token's logits stay on the device for acm_sample and are
+ * copied to logits_out (vocab floats) when it is non-NULL. */
+ACM_API int acm_forward(acm_model *m, int32_t seq, const int32_t *toks, int32_t n, float *logits_out);
+
+/* Sampler.Sample, sampler.go:30-76, on the device-resident logits of `seq`
+ * with the uniform draw of decode step `step`. */
+ACM_API int acm_sample(acm_model *m, int32_t seq, const acm_sampler *s, uint64_t step, int32_t *tok_out);
+
+/* One batched decode step for nseq independent sequences: Forward([in_tok[i]])
+ * on seqs[i], then Sample on the new logits with samplers[i] at steps[i].
+ * Writes the sampled ids to out_tok (and, when logits_out is non-NULL, the
+ * nseq x vocab logits).  The batched form of the loop body in sampler.go:136-157. */
+ACM_API int acm_decode_step(acm_model *m, int32_t nseq, const int32_t *seqs, const int32_t *in_tok,
+                            const acm_sampler *samplers, const uint64_t *steps, int32_t *out_tok,
+                            float *logits_out);
+
+/* Model.Generate, sampler.go:108-157: prefill in chunks of <= 1024 then decode
+ * until EOS/EOS2 (stop_on_eos != 0) or max_tok tokens.  out_ids needs max_tok
+ * entries; *n_out receives the count.  stats may be NULL. */
+ACM_API int acm_generate(acm_model *m, int32_t seq, const int32_t *prompt, int32_t n_prompt,
+                         const acm_sampler *s, int32_t max_tok, int32_t stop_on_eos, int32_t *out_ids,
+                         int32_t *n_out, acm_stats *stats);
+
+/* MaxLogit, model.go:462-471 (host helper, first maximum wins). */
+ACM_API int32_t acm_max_logit(const float *logits, int32_t n);
+
+/* ---- kernel-level entry points (parity tests and the kernel bench) ---- */
+
+/* Dequantize nrows rows of K elements with the device dequantizer
+ * (dequantRowSlow, tensor.go:55-81); host buffers in and out. */
+ACM_API int acm_dequant(acm_engine *e, uint32_t ggml_type, const void *host_bytes, int64_t nrows, int64_t k,
+                        float *host_out);
+
+/* matmul / matvec (tensor.go:253-303): y[m][n] = x[m][:] . W[n][:] with the
+ * engine's kernels (fused dequant-GEMV for m <= 8, dequant-GEMM otherwise);
+ * host buffers in and out. */
+ACM_API int acm_matmul(acm_engine *e, uint32_t ggml_type, const void *host_w, int64_t n, int64_t k,
+                       const float *host_x, int32_t m, float *host_y);
+
+/* The same on device pointers, enqueued on the engine stream (no copies, no
+ * synchronisation).  d_w must hold the tensor bytes at a 256-byte aligned
+ * address followed by at least 16 readable bytes. */
+ACM_API int acm_matmul_dev(acm_engine *e, uint32_t ggml_type, const void *d_w, int64_t n, int64_t k,
+                           const float *d_x, int32_t m, float *d_y);
+
+/* Sample from host logits with the device sampler (sampler parity tests). */
+ACM_API int acm_sample_logits(acm_engine *e, const float *host_logits, int32_t n, const acm_sampler *s,
+                              uint64_t step, int32_t *tok_out);
+
+/* Engine stream (cudaStream_t) and synchronisation, for callers that time
+ * device work with their own events. */
+ACM_API void *acm_engine_stream(acm_engine *e);
+ACM_API int acm_engine_sync(acm_engine *e);
+
+/* Device time in seconds of the last acm_forward / acm_generate phases,
+ * measured with CUDA events on the model stream. */
+ACM_API int acm_model_last_timing(acm_model *m, double *prefill_s, double *decode_s);
+
+/* Number of kernels the library has launched in this process (a CUDA-graph
+ * replay counts every kernel the graph holds).  No reference counterpart. */
+ACM_API uint64_t acm_kernel_launches(void);
+
+/* Measurement helper, no reference counterpart: replay the fused
+ * dequant-GEMV launches of one batch-1 decode token on this model's weights
+ * (q/k/v, o, gate/up, down of every layer, then lm_head -- the matvec calls of
+ * model.go:346-348, :410, :418-419, :423, :440) `reps` times from a CUDA
+ * graph and report the device seconds and algorithmic bytes (weight blocks +
+ * activation reads + output writes) per pass and the launches per pass. */
+ACM_API int acm_model_bench_gemv(acm_model *m, int32_t reps, double *sec_per_pass, double *bytes_per_pass,
+                                 int32_t *launches_per_pass);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ACM_H */

@@ -1,0 +1,108 @@
+"""Kernel parity on the GPU through the C ABI (acm_dequant / acm_matmul /
+acm_sample_logits) against the CPU oracle.
+
+Tolerances: dequant bit-exact (tensor.go:55-226 is exact in fp32; the
+reference pins asm vs scalar at 0 difference, cmp_test.go:37-40); matmul
+relative L2 <= 2e-6 against a float64 product of the exact dequantized
+weights (fp32 accumulation in a different order); sampler ids identical.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import rel_l2, same_bits
+
+pytestmark = pytest.mark.gpu
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden", "dequant_golden.npz")
+TYPES = {"f32": 0, "f16": 1, "q4_0": 2, "q5_0": 6, "q8_0": 8, "q4_k": 12, "q5_k": 13, "q6_k": 14}
+QTYPES = [2, 6, 8, 12, 13, 14]
+
+
+@pytest.fixture(scope="module")
+def eng(acm):
+    e = acm.Engine(0)
+    yield e
+    e.close()
+
+
+@pytest.mark.parametrize("name", list(TYPES))
+@pytest.mark.parametrize("kind", ["quant", "random"])
+def test_dequant_golden(eng, name, kind):
+    g = np.load(GOLD)
+    rows, k = int(g["rows"]), int(g["k"])
+    got = eng.dequant(TYPES[name], g[f"{name}_{kind}_in"].tobytes(), rows, k)
+    assert same_bits(got, g[f"{name}_{kind}_out"]).all()
+
+
+@pytest.mark.parametrize("typ", list(TYPES.values()))
+@pytest.mark.parametrize("rows,k", [(37, 1024), (5, 3072), (3, 2048)])
+def test_dequant_random_blocks(eng, oracle, synth, typ, rows, k):
+    data = synth.random_blocks(typ, rows, k, seed=typ * 31 + rows)
+    assert same_bits(eng.dequant(typ, data, rows, k), oracle.dequant(typ, data, rows, k)).all()
+
+
+def _check_matmul(eng, oracle, synth, typ, n, k, m, seed, tol=2e-6):
+    rng = np.random.default_rng(seed)
+    w = synth.quantize(typ, rng.standard_normal((n, k)).astype(np.float32) * 0.02)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    got = eng.matmul(typ, w, n, k, x)
+    want = x.astype(np.float64) @ oracle.dequant(typ, w, n, k).astype(np.float64).T
+    assert got.shape == (m, n)
+    assert rel_l2(got, want) < tol
+    for j in range(m):  # every token row individually
+        assert rel_l2(got[j], want[j]) < 5 * tol
+
+
+@pytest.mark.parametrize("typ", list(TYPES.values()))
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8])
+def test_gemv(eng, oracle, synth, typ, m):
+    _check_matmul(eng, oracle, synth, typ, 300, 1024, m, seed=typ + 10 * m)
+
+
+@pytest.mark.parametrize("typ", list(TYPES.values()))
+@pytest.mark.parametrize("n,k", [(77, 3072), (1000, 256), (64, 8192)])
+def test_gemv_shapes(eng, oracle, synth, typ, n, k):
+    _check_matmul(eng, oracle, synth, typ, n, k, 1, seed=n + k + typ)
+
+
+@pytest.mark.parametrize("typ", list(TYPES.values()))
+@pytest.mark.parametrize("m", [9, 64, 130])
+def test_gemm(eng, oracle, synth, typ, m):
+    _check_matmul(eng, oracle, synth, typ, 200, 512, m, seed=typ * 3 + m)
+
+
+@pytest.mark.parametrize("typ", QTYPES)
+@pytest.mark.parametrize("shape", [(1024, 2048), (2048, 1024), (1024, 3072), (3072, 1024)])
+def test_microbench_shapes(eng, oracle, synth, typ, shape):
+    """The kernel-microbench weight shapes [K x N] at activation batch 1."""
+    k, n = shape
+    _check_matmul(eng, oracle, synth, typ, n, k, 1, seed=k * 7 + n + typ)
+
+
+def _logits(v, seed, ties=True):
+    rng = np.random.default_rng(seed)
+    lg = rng.standard_normal(v).astype(np.float32) * 2
+    if ties:  # repeated maxima and repeated values across chunk boundaries
+        top = lg.max() + 1
+        lg[[5, 4000, 150000 % v, v - 1]] = top
+        lg[rng.integers(0, v, 200)] = np.float32(1.25)
+    return lg
+
+
+@pytest.mark.parametrize("v", [1000, 151936, 128256])
+def test_sampler_greedy(eng, oracle, acm, v):
+    for seed in range(3):
+        lg = _logits(v, seed)
+        assert eng.sample_logits(lg, acm.Sampler(0.0), 0) == oracle.sample(lg, 0.0, 0, 0.0, 0.5)
+
+
+@pytest.mark.parametrize("v", [1000, 151936])
+@pytest.mark.parametrize("temp,top_k,top_p", [(0.7, 40, 0.0), (1.0, 0, 0.9), (0.5, 64, 0.0), (1.3, 5, 0.5)])
+def test_sampler_topk(eng, oracle, acm, v, temp, top_k, top_p):
+    for step in range(20):
+        lg = _logits(v, 100 + step, ties=step % 2 == 0)
+        s = acm.Sampler(temp, top_k, top_p, Seed=1000 + step)
+        want = oracle.sample(lg, temp, top_k, top_p, oracle.uniform(1000 + step, step))
+        assert eng.sample_logits(lg, s, step) == want
