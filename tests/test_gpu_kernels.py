@@ -86,7 +86,7 @@ def _logits(v, seed, ties=True):
     lg = rng.standard_normal(v).astype(np.float32) * 2
     if ties:  # repeated maxima and repeated values across chunk boundaries
         top = lg.max() + 1
-        lg[[5, 4000, 150000 % v, v - 1]] = top
+        lg[[5, 4000 % v, 150000 % v, v - 1]] = top
         lg[rng.integers(0, v, 200)] = np.float32(1.25)
     return lg
 
