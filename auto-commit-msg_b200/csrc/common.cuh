@@ -58,6 +58,33 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// Programmatic dependent launch: wait for the preceding kernel in the stream
+// (all its memory operations visible), and allow the next one to start its
+// CTAs early.  Both are no-ops when the launch did not opt in.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Order-preserving 64-bit key of (logit, index): descending key order is
+// descending logit, and among equal logits ascending index -- the tie rule of
+// greedy() and topK() (sampler.go:19-27, :80-98).  NaN ranks last.
+__device__ __forceinline__ unsigned long long logit_key(float v, int idx) {
+    const uint32_t b = __float_as_uint(v);
+    uint32_t o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    if (v != v) o = 0;
+    return ((unsigned long long)o << 32) | (uint32_t)(0xFFFFFFFFu - (uint32_t)idx);
+}
+__device__ __forceinline__ float key_logit(unsigned long long k) {
+    const uint32_t o = (uint32_t)(k >> 32);
+    return __uint_as_float((o & 0x80000000u) ? (o & 0x7FFFFFFFu) : ~o);
+}
+__device__ __forceinline__ int key_index(unsigned long long k) { return (int)(0xFFFFFFFFu - (uint32_t)k); }
+
+// 16-byte asynchronous global -> shared copy (L2 only) and its wait.
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // Named barrier among `nthreads` threads (a subset of the CTA).
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

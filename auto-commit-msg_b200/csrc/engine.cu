@@ -138,6 +138,9 @@ struct acm_model {
     double *d_temp = nullptr, *d_topp = nullptr;
     uint64_t *d_seed = nullptr, *d_step = nullptr, *d_cand = nullptr;
     int32_t *d_hist = nullptr, *d_hist_col = nullptr;
+    unsigned long long *d_amax = nullptr;  // per-token argmax keys (greedy decode)
+    int *d_attn_cnt = nullptr;              // decode attention split counters
+    int dec_nsplit = 1;                     // chunk capacity of the decode attention
     int nchunks = 0;
     Pinned<int32_t> h_tok, h_seq, h_pos, h_out, h_topk, h_hist;
     Pinned<double> h_temp, h_topp;
@@ -234,7 +237,11 @@ int attn_nsplit(acm_model *m, int ntok, int max_pos) {
 // One pass over `ntok` tokens whose ids/slots/positions are already in
 // d_tok/d_seq/d_pos.  Logits are produced for tokens [lm_first, lm_first +
 // lm_count) into their slots' rows of m->logits.  Enqueues only (capturable).
-int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count) {
+// `decode`: every token belongs to a different sequence (one new token each),
+// which enables the fused decode attention; `amax`: fold the lm_head rows
+// into per-token argmax keys (greedy sampling) instead of only storing logits.
+int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count, bool decode = false,
+                 unsigned long long *amax = nullptr) {
     const acm_config &c = m->c;
     cudaStream_t st = m->e->stream;
     const int E = c.n_embd, hd = c.head_dim, qd = c.n_head * hd, kvd = c.n_head_kv * hd, F = c.n_ff;
@@ -263,9 +270,14 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
         }
         RopeDesc rd{m->q, m->k, m->v, L.q_nw, L.k_nw, m->rope_tab, c.n_head, c.n_head_kv, hd, c.rope_dim,
                     c.rope_interleaved, eps};
-        CK_M(rope_append_launch(rd, kv, l, tm, ntok, st));
-        AttnDesc ad{m->q, m->att, c.n_head, c.n_head_kv, hd, scale, m->part, nsplit};
-        CK_M(attention_launch(ad, kv, l, tm, ntok, max_pos, st));
+        if (decode) {
+            AttnDesc ad{m->q, m->att, c.n_head, c.n_head_kv, hd, scale, m->part, m->dec_nsplit, m->d_attn_cnt};
+            CK_M(attention_decode_launch(rd, ad, kv, l, tm, ntok, max_pos, st));
+        } else {
+            CK_M(rope_append_launch(rd, kv, l, tm, ntok, st));
+            AttnDesc ad{m->q, m->att, c.n_head, c.n_head_kv, hd, scale, m->part, nsplit, nullptr};
+            CK_M(attention_launch(ad, kv, l, tm, ntok, max_pos, st));
+        }
         // x += Wo att
         if (gemv_supported(L.o->type, qd, ntok)) {
             GemvSegDesc so{L.o->d, nullptr, (int)L.o->type, E, EPI_ADD, m->x, E, nullptr, nullptr};
@@ -309,7 +321,7 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
         const int V = (int)m->out->rows();
         if (gemv_supported(m->out->type, E, lm_count)) {
             GemvSegDesc so{m->out->d, nullptr, (int)m->out->type, V, EPI_STORE, m->logits, c.vocab, nullptr,
-                           m->d_seq + lm_first};
+                           m->d_seq + lm_first, amax};
             CK_M(gemv_launch(&so, 1, xin, E, E, lm_count, m->out_nw, eps, S, st));
         } else {
             CK_M(rmsnorm_launch(xin, E, m->out_nw, m->h, E, lm_count, E, eps, st));
@@ -354,17 +366,20 @@ int decode_graph_launch(acm_model *m, int ntok, bool greedy) {
     cudaStream_t st = m->e->stream;
     if (it == m->graphs.end()) {
         // warm-up run outside capture (first launches set kernel attributes)
-        int rc = forward_pass(m, ntok, m->c.max_ctx - 1, 0, ntok);
+        int rc = forward_pass(m, ntok, m->c.max_ctx - 1, 0, ntok, true, greedy ? m->d_amax : nullptr);
         if (rc) return rc;
-        if ((rc = sample_pass(m, ntok, greedy))) return rc;
+        if (!greedy && (rc = sample_pass(m, ntok, greedy))) return rc;
+        CK_M(cudaMemsetAsync(m->d_amax, 0, sizeof(unsigned long long) * ntok, st));
         if ((rc = sync_check(m))) return rc;
         cudaGraph_t g = nullptr;
         const unsigned long long before = g_kernel_launches.load();
         CK_M(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-        rc = forward_pass(m, ntok, m->c.max_ctx - 1, 0, ntok);
-        if (!rc) rc = sample_pass(m, ntok, greedy);
-        cudaError_t ae = advance_launch(m->d_tok, m->d_pos, m->d_step, m->d_out, m->d_hist, HIST_MAX, m->d_hist_col,
-                                        ntok, st);
+        // greedy: the lm_head epilogue keeps the argmax and advance reads it;
+        // otherwise the top-k sampler runs between them
+        rc = forward_pass(m, ntok, m->c.max_ctx - 1, 0, ntok, true, greedy ? m->d_amax : nullptr);
+        if (!rc && !greedy) rc = sample_pass(m, ntok, greedy);
+        cudaError_t ae = advance_launch(m->d_tok, m->d_pos, m->d_step, m->d_out, greedy ? m->d_amax : nullptr,
+                                        m->d_hist, HIST_MAX, m->d_hist_col, ntok, st);
         cudaError_t ce = cudaStreamEndCapture(st, &g);
         const unsigned long long captured = g_kernel_launches.load() - before;
         g_kernel_launches -= captured;  // capturing is not executing
@@ -430,7 +445,7 @@ int forward_seq(acm_model *m, int seq, const int32_t *toks, int n) {
         }
         if ((rc = upload_meta(m, cnt))) return rc;
         const bool last = i + cnt == n;
-        if ((rc = forward_pass(m, cnt, s.pos + i + cnt - 1, cnt - 1, last ? 1 : 0))) return rc;
+        if ((rc = forward_pass(m, cnt, s.pos + i + cnt - 1, cnt - 1, last ? 1 : 0, cnt == 1))) return rc;
     }
     s.pos += n;
     return ACM_OK;
@@ -651,7 +666,11 @@ ACM_API int acm_model_finalize(acm_model *m) {
     CK_M(dalloc(m, &m->att, T * qd));
     CK_M(dalloc(m, &m->hb, T * F));
     CK_M(dalloc(m, &m->hb2, T * F));
-    CK_M(dalloc(m, &m->part, (size_t)PART_TOKSPLIT * c.n_head * (hd + 2)));
+    m->dec_nsplit = (c.max_ctx + 31) / 32;  // 32-position chunks of the decode attention
+    const size_t part_rows = std::max<size_t>((size_t)PART_TOKSPLIT, (size_t)m->tdec * m->dec_nsplit);
+    CK_M(dalloc(m, &m->part, part_rows * c.n_head * (hd + 2)));
+    CK_M(dalloc(m, &m->d_attn_cnt, (size_t)m->tdec * c.n_head_kv));
+    CK_M(cudaMemset(m->d_attn_cnt, 0, sizeof(int) * (size_t)m->tdec * c.n_head_kv));
     CK_M(dalloc(m, &m->logits, (size_t)m->max_seqs * c.vocab));
     CK_M(cudaMemset(m->logits, 0, sizeof(float) * (size_t)m->max_seqs * c.vocab));
     CK_M(dalloc(m, &m->d_tok, T));
@@ -667,6 +686,8 @@ ACM_API int acm_model_finalize(acm_model *m) {
     CK_M(dalloc(m, &m->d_cand, (size_t)m->tdec * m->nchunks * 64));
     CK_M(dalloc(m, &m->d_hist, (size_t)m->tdec * HIST_MAX));
     CK_M(dalloc(m, &m->d_hist_col, 1));
+    CK_M(dalloc(m, &m->d_amax, T));
+    CK_M(cudaMemset(m->d_amax, 0, sizeof(unsigned long long) * T));
     CK_M(m->h_tok.alloc(T));
     CK_M(m->h_seq.alloc(T));
     CK_M(m->h_pos.alloc(T));

@@ -15,6 +15,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 #include "quant.cuh"
 
 namespace acm {
@@ -27,6 +28,8 @@ __device__ __forceinline__ const float *kv_row(const float *pool, const KVDesc &
 template <int HD>
 __global__ void __launch_bounds__(128) k_attn(const AttnDesc a, const KVDesc kv, int layer, TokMeta tm,
                                               int chunk_max) {
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
     extern __shared__ float sm[];
     constexpr int PER = HD / 32;  // q/k elements per lane
     const int t = blockIdx.x, g = blockIdx.y, split = blockIdx.z;
@@ -137,6 +140,8 @@ __global__ void __launch_bounds__(128) k_attn(const AttnDesc a, const KVDesc kv,
 // w_s = fastExp(m_s - max_s m_s).
 template <int HD>
 __global__ void k_attn_combine(const AttnDesc a) {
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
     const int t = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
     const float *pp = a.part + ((int64_t)t * a.n_head + h) * a.nsplit * (HD + 2);
     float mx = -FLT_MAX;
@@ -152,6 +157,221 @@ __global__ void k_attn_combine(const AttnDesc a) {
         }
     }
     a.out[(int64_t)t * a.n_head * HD + (int64_t)h * HD + d] = num / den;
+}
+
+// ---------------------------------------------------------------------------
+// Decode attention with the new token's QK-norm / RoPE / cache append fused
+// in.  Tokens belong to distinct sequences.  CTA (t, g, c) covers positions
+// [32c, 32c + 32) of token t's sequence for kv head g; CTAs past the
+// sequence's length exit at once.  Each CTA stages its K/V rows in shared
+// memory with asynchronous copies issued together, rotates its G query heads
+// itself, and -- when its range holds the new position -- normalises and
+// rotates the new key, writes key and value to the cache and uses them
+// directly.  With one chunk the CTA writes the normalised output; otherwise
+// it writes (sum e*v, max, sum e) and the last CTA to arrive merges.
+// ---------------------------------------------------------------------------
+constexpr int ATT_CHUNK = 32;
+
+template <int HD>
+__device__ __forceinline__ void head_norm_rope(float *v, const float *nw, const RopeDesc &r, int pos, int lane) {
+    // v: HD floats in shared memory (one warp); rmsnorm (model.go:213-222)
+    // then rope (model.go:237-251) in place
+    if (nw) {
+        float ss = 0.f;
+        for (int d = lane; d < HD; d += 32) ss = fmaf(v[d], v[d], ss);
+        ss = warp_sum(ss);
+        const float sc = rms_scale(ss, HD, r.eps);
+        __syncwarp();
+        for (int d = lane; d < HD; d += 32) v[d] = __fmul_rn(__fmul_rn(v[d], sc), nw[d]);
+    }
+    __syncwarp();
+    const int half = r.rope_dim / 2;
+    const float2 *tab = r.tab + (int64_t)pos * half;
+    for (int i = lane; i < half; i += 32) {
+        const int ia = r.interleaved ? 2 * i : i, ib = r.interleaved ? 2 * i + 1 : i + half;
+        const float a = v[ia], b = v[ib];
+        const float2 cs = tab[i];
+        v[ia] = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+        v[ib] = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
+    }
+    __syncwarp();
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) k_attn_decode(const RopeDesc r, const AttnDesc a, const KVDesc kv, int layer,
+                                                     TokMeta tm) {
+    extern __shared__ float sm[];
+    constexpr int PER = HD / 32;
+    const int t = blockIdx.x, g = blockIdx.y, c = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = a.n_head / a.n_head_kv, nh = a.n_head, qd = nh * HD, kvd = a.n_head_kv * HD;
+    if (tid == 0) pdl_trigger();
+    pdl_wait();
+    const int seq = tm.seq[t], pos = tm.pos[t], L = pos + 1;
+    const int lo = c * ATT_CHUNK;
+    if (lo >= L) return;
+    const int hi = min(L, lo + ATT_CHUNK), n = hi - lo;
+    const int nchunk = (L + ATT_CHUNK - 1) / ATT_CHUNK;
+    float *qs = sm;                       // [G][HD]
+    float *ks = qs + G * HD;              // [ATT_CHUNK][HD]
+    float *vs = ks + ATT_CHUNK * HD;      // [ATT_CHUNK][HD]
+    float *sc = vs + ATT_CHUNK * HD;      // [G][ATT_CHUNK]
+    float *stat = sc + G * ATT_CHUNK;     // [G][2]
+    float *red = stat + 2 * G;            // [G][HD] second position group (HD = 64)
+    int *flag = reinterpret_cast<int *>(red + G * HD);
+    const bool has_new = pos >= lo && pos < hi;
+    // stage the cached rows (all copies in flight together)
+    const int ncopy = has_new ? n - 1 : n;
+    constexpr int CPR = HD / 4;  // 16-byte pieces per row
+    // the chunk lies in one page (ATT_CHUNK divides the page size): one lookup
+    const int64_t base = (int64_t)layer * kv.layer_stride +
+                         ((int64_t)kv.page_table[(int64_t)seq * kv.max_pages + lo / kv.page_size] * kv.page_size +
+                          (lo % kv.page_size)) * kv.kvd + g * HD;
+    for (int i = tid; i < ncopy * CPR * 2; i += 128) {
+        const int which = i / (ncopy * CPR), rem = i - which * ncopy * CPR;
+        const int p = rem / CPR, piece = rem - p * CPR;
+        const float *row = (which ? kv.v : kv.k) + base + (int64_t)p * kv.kvd;
+        cp_async16((which ? vs : ks) + p * HD + piece * 4, row + piece * 4);
+    }
+    // query heads of this group: norm + rope (each chunk CTA redoes this)
+    for (int h = warp; h < G; h += 4) {
+        const float *src = a.q + (int64_t)t * qd + (int64_t)(g * G + h) * HD;
+        for (int d = lane; d < HD; d += 32) qs[h * HD + d] = src[d];
+        __syncwarp();
+        head_norm_rope<HD>(qs + h * HD, r.q_nw, r, pos, lane);
+    }
+    if (has_new && warp == (G & 3)) {
+        // the new position: k = rope(norm(k)), v as produced; into the cache
+        float *kn = ks + (n - 1) * HD, *vn = vs + (n - 1) * HD;
+        const float *ksrc = r.k + (int64_t)t * kvd + g * HD, *vsrc = r.v + (int64_t)t * kvd + g * HD;
+        for (int d = lane; d < HD; d += 32) {
+            kn[d] = ksrc[d];
+            vn[d] = vsrc[d];
+        }
+        __syncwarp();
+        head_norm_rope<HD>(kn, r.k_nw, r, pos, lane);
+        float *kd = const_cast<float *>(kv_row(kv.k, kv, layer, seq, pos)) + g * HD;
+        float *vd = const_cast<float *>(kv_row(kv.v, kv, layer, seq, pos)) + g * HD;
+        for (int d = lane; d < HD; d += 32) {
+            kd[d] = kn[d];
+            vd[d] = vn[d];
+        }
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    // scores
+    for (int p = warp; p < n; p += 4) {
+        float kk[PER];
+#pragma unroll
+        for (int e = 0; e < PER; e++) kk[e] = ks[p * HD + lane + 32 * e];
+        for (int h = 0; h < G; h++) {
+            float s = 0.f;
+#pragma unroll
+            for (int e = 0; e < PER; e++) s = fmaf(qs[h * HD + lane + 32 * e], kk[e], s);
+            s = warp_sum(s);
+            if (lane == 0) sc[h * ATT_CHUNK + p] = __fmul_rn(s, a.scale);
+        }
+    }
+    __syncthreads();
+    for (int h = warp; h < G; h += 4) {
+        float *s = sc + h * ATT_CHUNK;
+        float mx = -FLT_MAX;
+        for (int i = lane; i < n; i += 32) mx = fmaxf(mx, s[i]);
+        mx = warp_max(mx);
+        float sum = 0.f;
+        for (int i = lane; i < n; i += 32) {
+            const float e = fast_exp(__fsub_rn(s[i], mx));
+            s[i] = e;
+            sum += e;
+        }
+        sum = warp_sum(sum);
+        __syncwarp();
+        if (nchunk == 1)
+            for (int i = lane; i < n; i += 32) s[i] = __fdiv_rn(s[i], sum);
+        if (lane == 0) {
+            stat[2 * h] = mx;
+            stat[2 * h + 1] = sum;
+        }
+    }
+    __syncthreads();
+    constexpr int GROUPS = 128 / HD;
+    const int d = tid % HD, grp = tid / HD;
+    float acc[8];
+#pragma unroll
+    for (int h = 0; h < 8; h++) acc[h] = 0.f;
+    for (int p = grp; p < n; p += GROUPS) {
+        const float v = vs[p * HD + d];
+#pragma unroll
+        for (int h = 0; h < 8; h++)
+            if (h < G) acc[h] = fmaf(sc[h * ATT_CHUNK + p], v, acc[h]);
+    }
+    if (GROUPS > 1) {
+        if (grp > 0)
+            for (int h = 0; h < G; h++) red[h * HD + d] = acc[h];
+        __syncthreads();
+        if (grp == 0)
+            for (int h = 0; h < G; h++) acc[h] += red[h * HD + d];
+    }
+    if (nchunk == 1) {
+        if (grp == 0)
+            for (int h = 0; h < G; h++) a.out[(int64_t)t * qd + (int64_t)(g * G + h) * HD + d] = acc[h];
+        return;
+    }
+    // partial for this chunk; the last chunk CTA to arrive merges
+    if (grp == 0)
+        for (int h = 0; h < G; h++) {
+            float *pp = a.part + (((int64_t)t * nh + g * G + h) * a.nsplit + c) * (HD + 2);
+            pp[d] = acc[h];
+            if (d == 0) {
+                pp[HD] = stat[2 * h];
+                pp[HD + 1] = stat[2 * h + 1];
+            }
+        }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        int *cnt = a.counter + (int64_t)t * a.n_head_kv + g;
+        const int old = atomicAdd(cnt, 1);
+        const int last = old == nchunk - 1;
+        if (last) *cnt = 0;  // ready for the next step
+        *flag = last;
+    }
+    __syncthreads();
+    if (!*flag) return;
+    __threadfence();
+    if (grp != 0) return;
+    for (int h = 0; h < G; h++) {
+        const float *pp = a.part + ((int64_t)t * nh + g * G + h) * a.nsplit * (HD + 2);
+        float mx = -FLT_MAX;
+#pragma unroll 8
+        for (int s = 0; s < nchunk; s++) mx = fmaxf(mx, __ldcg(pp + s * (HD + 2) + HD));
+        float num = 0.f, den = 0.f;
+#pragma unroll 8
+        for (int s = 0; s < nchunk; s++) {
+            const float w = fast_exp(__ldcg(pp + s * (HD + 2) + HD) - mx);
+            num = fmaf(w, __ldcg(pp + s * (HD + 2) + d), num);
+            den = fmaf(w, __ldcg(pp + s * (HD + 2) + HD + 1), den);
+        }
+        a.out[(int64_t)t * qd + (int64_t)(g * G + h) * HD + d] = num / den;
+    }
+}
+
+cudaError_t attention_decode_launch(const RopeDesc &r, const AttnDesc &a, const KVDesc &kv, int layer, TokMeta tm,
+                                    int ntok, int max_pos, cudaStream_t st) {
+    if (ntok <= 0) return cudaSuccess;
+    const int G = a.n_head / a.n_head_kv;
+    if (G > 8 || a.n_head % a.n_head_kv || (a.head_dim != 64 && a.head_dim != 128)) return cudaErrorInvalidValue;
+    const int nchunk = (max_pos + 1 + ATT_CHUNK - 1) / ATT_CHUNK;
+    if (nchunk > a.nsplit) return cudaErrorInvalidValue;  // partial buffer capacity
+    if (kv.page_size % ATT_CHUNK) return cudaErrorInvalidValue;
+    const int HD = a.head_dim;
+    const size_t smem = ((size_t)G * HD + 2 * ATT_CHUNK * HD + (size_t)G * ATT_CHUNK + 2 * G + (size_t)G * HD + 4) *
+                        sizeof(float);
+    dim3 grid(ntok, a.n_head_kv, nchunk);
+    cudaError_t e = HD == 128 ? launch_pdl(k_attn_decode<128>, grid, dim3(128), smem, st, r, a, kv, layer, tm)
+                              : launch_pdl(k_attn_decode<64>, grid, dim3(128), smem, st, r, a, kv, layer, tm);
+    if (e != cudaSuccess) return e;
+    return launched(1);
 }
 
 cudaError_t attention_launch(const AttnDesc &a, const KVDesc &kv, int layer, TokMeta tm, int ntok, int max_pos,
@@ -174,15 +394,15 @@ cudaError_t attention_launch(const AttnDesc &a, const KVDesc &kv, int layer, Tok
             cudaFuncSetAttribute(k_attn<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
             attr[dev & 63][0] = true;
         }
-        k_attn<128><<<grid, 128, smem, st>>>(a, kv, layer, tm, chunk_max);
-        if (a.nsplit > 1) k_attn_combine<128><<<dim3(ntok, a.n_head), 128, 0, st>>>(a);
+        launch_pdl(k_attn<128>, grid, dim3(128), smem, st, a, kv, layer, tm, chunk_max);
+        if (a.nsplit > 1) launch_pdl(k_attn_combine<128>, dim3(ntok, a.n_head), dim3(128), 0, st, a);
     } else if (HD == 64) {
         if (!attr[dev & 63][1]) {
             cudaFuncSetAttribute(k_attn<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
             attr[dev & 63][1] = true;
         }
-        k_attn<64><<<grid, 128, smem, st>>>(a, kv, layer, tm, chunk_max);
-        if (a.nsplit > 1) k_attn_combine<64><<<dim3(ntok, a.n_head), 64, 0, st>>>(a);
+        launch_pdl(k_attn<64>, grid, dim3(128), smem, st, a, kv, layer, tm, chunk_max);
+        if (a.nsplit > 1) launch_pdl(k_attn_combine<64>, dim3(ntok, a.n_head), dim3(64), 0, st, a);
     } else {
         return cudaErrorInvalidValue;
     }

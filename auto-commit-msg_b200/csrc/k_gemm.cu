@@ -10,6 +10,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 #include "quant.cuh"
 
 namespace acm {
@@ -20,6 +21,8 @@ constexpr int GPAD = 4;
 
 template <int T, bool PAIR>
 __global__ void __launch_bounds__(256) k_gemm_simt(const GemmDesc d) {
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
     extern __shared__ __align__(16) float gsm[];
     float(*As)[GB + GPAD] = reinterpret_cast<float(*)[GB + GPAD]>(gsm);
     float(*Ws)[GK][GB + GPAD] = reinterpret_cast<float(*)[GK][GB + GPAD]>(gsm + GK * (GB + GPAD));
@@ -147,8 +150,8 @@ cudaError_t gemm_launch(const GemmDesc &d, cudaStream_t st) {
     switch (d.type) {
 #define ACM_GM(T)                                                       \
     case T:                                                             \
-        if (pair) k_gemm_simt<T, true><<<grid, 256, smem, st>>>(d);     \
-        else k_gemm_simt<T, false><<<grid, 256, smem, st>>>(d);         \
+        if (pair) launch_pdl(k_gemm_simt<T, true>, grid, dim3(256), smem, st, d);     \
+        else launch_pdl(k_gemm_simt<T, false>, grid, dim3(256), smem, st, d);         \
         break;
         ACM_GM(T_F32) ACM_GM(T_F16) ACM_GM(T_Q4_0) ACM_GM(T_Q5_0) ACM_GM(T_Q8_0) ACM_GM(T_Q4_K) ACM_GM(T_Q5_K)
         ACM_GM(T_Q6_K)

@@ -7,28 +7,59 @@
 //   * one CTA per SM; each CTA owns a contiguous row range of one weight
 //     matrix (several matrices -- q/k/v, gate/up -- share one launch);
 //   * a producer warp moves whole rows into a ring of shared-memory stages
-//     with the bulk-copy engine (cp.async.bulk + mbarrier), so every CTA has
-//     tens of KB of HBM reads in flight from its first cycle;
-//   * 8 consumer warps take one row at a time; lane l decodes units l, l+32,
-//     ... (32 elements each) against the activation vector, which the CTA
-//     stores in shared memory permuted into unit order (and optionally
-//     RMS-normalised first: the norm before q/k/v, gate/up and lm_head);
-//   * the row sum is a warp-shuffle reduction; the epilogue stores, adds to
-//     the residual stream, or applies SwiGLU to a gate/up pair.
+//     with the bulk-copy engine (cp.async.bulk + mbarrier).  It starts before
+//     the kernel waits on its predecessor (programmatic dependent launch):
+//     weights never depend on earlier kernels, so their HBM reads overlap the
+//     previous kernel's tail;
+//   * consumer warps decode the staged rows.  Unit path (small matrices): a
+//     warp per row, lane l decodes 32-element units l, l+32, ... against the
+//     activations permuted into unit order.  Wide path (large matrices such
+//     as lm_head): `lpr` lanes per row, each decoding whole 256-element
+//     super-blocks so block headers are read once per 256 weights;
+//   * the row sum is a shuffle reduction; the epilogue stores, adds to the
+//     residual stream, applies SwiGLU to a gate/up pair, or (lm_head under
+//     greedy sampling) folds the row into a per-token argmax key.
 #include <stdio.h>
+#include <stdlib.h>
 
 #include <algorithm>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 #include "quant.cuh"
+#include "sbdot.cuh"
 
 namespace acm {
 
 __device__ int g_dev_error = 0;  // declared in common.cuh (relocatable device code)
+bool g_pdl = [] {
+    const char *e = getenv("ACM_PDL");
+    return !(e && e[0] == '0');
+}();
+
+template <int MT>
+struct Cfg {
+    static constexpr int NCW = MT <= 2 ? 16 : 8;  // consumer warps
+    static constexpr int NT = NCW * 32 + 32;      // + producer warp
+};
+
+// Shared layout: [bars 128 B][x area][xsum area][red 16*MT floats][stages].
+// Unit path x area: MT*K floats permuted into unit order, xsum MT*(K/32)
+// float2 (low/high half sums per unit).  Wide path x area: MT*(K/256)*260
+// floats (natural order, 4 floats of padding per 256), xsum MT*(K/32) floats.
+__host__ __device__ inline size_t x_area_floats(int64_t k, int mt, int lpr) {
+    return lpr ? (size_t)mt * (k / 256) * 260 : (size_t)mt * k;
+}
+__host__ __device__ inline size_t x_bytes(int64_t k, int mt, int lpr) {
+    size_t b = 128 + x_area_floats(k, mt, lpr) * 4 + (size_t)mt * (k / 32) * 8 + 16 * mt * 4;
+    return (b + 127) & ~size_t(127);
+}
 
 template <int T, int MT>
-__device__ __forceinline__ void prep_x(const GemvArgs &a, float *xs, float2 *xsum, float *red) {
+__device__ __forceinline__ void prep_x(const GemvArgs &a, float *xs, float *xsum, float *red) {
+    constexpr int NCW = Cfg<MT>::NCW, NC = NCW * 32;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = a.k;
     float sc[MT];
@@ -38,31 +69,38 @@ __device__ __forceinline__ void prep_x(const GemvArgs &a, float *xs, float2 *xsu
         float ss[MT];
 #pragma unroll
         for (int m = 0; m < MT; m++) ss[m] = 0.f;
-        for (int k = tid; k < K; k += 256)
+        for (int k = tid; k < K; k += NC)
 #pragma unroll
             for (int m = 0; m < MT; m++)
                 if (m < a.m) {
-                    float v = a.x[(int64_t)m * a.ldx + k];
+                    const float v = a.x[(int64_t)m * a.ldx + k];
                     ss[m] = fmaf(v, v, ss[m]);
                 }
 #pragma unroll
         for (int m = 0; m < MT; m++) {
-            float w = warp_sum(ss[m]);
+            const float w = warp_sum(ss[m]);
             if (lane == 0) red[warp * MT + m] = w;
         }
-        named_sync(1, 256);
+        named_sync(1, NC);
 #pragma unroll
         for (int m = 0; m < MT; m++) {
             float t = 0.f;
-            for (int w = 0; w < 8; w++) t += red[w * MT + m];
+            for (int w = 0; w < NCW; w++) t += red[w * MT + m];
             sc[m] = rms_scale(t, K, a.eps);
         }
     }
-    for (int k = tid; k < K; k += 256) {
-        int u, j;
-        pos_unit<T>(k, K, u, j);
-        const int off = u * 32 + (((j >> 2) ^ (u & 7)) << 2) + (j & 3);
+    const bool wide = a.lpr != 0;
+    for (int k = tid; k < K; k += NC) {
+        int off;
+        if (wide) {
+            off = (k >> 8) * 260 + (k & 255);
+        } else {
+            int u, j;
+            pos_unit<T>(k, K, u, j);
+            off = u * 32 + (((j >> 2) ^ (u & 7)) << 2) + (j & 3);
+        }
         const float nw = a.norm_w ? a.norm_w[k] : 1.0f;
+        const size_t xstr = wide ? (size_t)(K / 256) * 260 : (size_t)K;
 #pragma unroll
         for (int m = 0; m < MT; m++) {
             float v = 0.f;
@@ -70,13 +108,29 @@ __device__ __forceinline__ void prep_x(const GemvArgs &a, float *xs, float2 *xsu
                 v = a.x[(int64_t)m * a.ldx + k];
                 if (a.norm_w) v = __fmul_rn(__fmul_rn(v, sc[m]), nw);
             }
-            xs[m * K + off] = v;
+            xs[m * xstr + off] = v;
         }
     }
-    named_sync(1, 256);
-    if constexpr (T == T_Q4_K || T == T_Q5_K) {
-        const int U = K / 32;
-        for (int idx = tid; idx < MT * U; idx += 256) {
+    named_sync(1, NC);
+    const int U = K / 32;
+    if (wide) {
+        // per-32 sums for the min terms of K-quants
+        const int xstr = (K / 256) * 260;
+        for (int idx = tid; idx < MT * U; idx += NC) {
+            const int m = idx / U, u = idx - m * U;
+            const float *p = xs + m * xstr + (u >> 3) * 260 + (u & 7) * 32;
+            float s = 0.f;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                const float4 v = *reinterpret_cast<const float4 *>(p + 4 * c);
+                s += (v.x + v.y) + (v.z + v.w);
+            }
+            xsum[m * U + u] = s;
+        }
+        named_sync(1, NC);
+    } else if constexpr (T == T_Q4_K || T == T_Q5_K) {
+        float2 *xs2 = reinterpret_cast<float2 *>(xsum);
+        for (int idx = tid; idx < MT * U; idx += NC) {
             const int m = idx / U, u = idx - m * U;
             const float *p = xs + m * K + u * 32;
             float lo = 0.f, hi = 0.f;
@@ -88,20 +142,65 @@ __device__ __forceinline__ void prep_x(const GemvArgs &a, float *xs, float2 *xsu
                 lo += (a0.x + a0.y) + (a0.z + a0.w);
                 hi += (a1.x + a1.y) + (a1.z + a1.w);
             }
-            xsum[m * U + u] = make_float2(lo, hi);
+            xs2[m * U + u] = make_float2(lo, hi);
         }
-        named_sync(1, 256);
+        named_sync(1, NC);
+    }
+}
+
+// Epilogue of one finished row n (values for tokens 0..m_used-1).
+template <int MT>
+__device__ __forceinline__ void row_out(const GemvSeg &s, int n, int m_used, const float (&acc)[MT],
+                                        const float (&acc2)[MT], unsigned long long (&best)[MT]) {
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+        if (m < m_used) {
+            float v = acc[m];
+            if (s.bias) v += s.bias[n];
+            float *yp = s.y + (int64_t)(s.yrow ? s.yrow[m] : m) * s.ldy + n;
+            if (s.epi == EPI_ADD) {
+                *yp += v;
+            } else if (s.epi == EPI_SWIGLU) {
+                const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, fast_exp(-v)));
+                *yp = __fmul_rn(__fmul_rn(v, sg), acc2[m]);
+            } else {
+                *yp = v;
+            }
+            if (s.amax) {
+                const unsigned long long k = logit_key(v, n);
+                best[m] = k > best[m] ? k : best[m];
+            }
+        }
+    }
+}
+
+template <int MT>
+__device__ __forceinline__ void flush_argmax(const GemvSeg &s, int m_used, unsigned long long (&best)[MT]) {
+    if (!s.amax) return;
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+        unsigned long long b = best[m];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long x = __shfl_xor_sync(0xffffffffu, b, o);
+            b = x > b ? x : b;
+        }
+        if ((threadIdx.x & 31) == 0 && m < m_used && b) atomicMax(&s.amax[m], b);
     }
 }
 
 template <int T, int MT>
-__device__ __forceinline__ void gemv_consume(const GemvArgs &a, const GemvSeg &s, int r0, int r1, uint64_t *full,
+__device__ __forceinline__ void consume_unit(const GemvArgs &a, const GemvSeg &s, int r0, int r1, uint64_t *full,
                                              uint64_t *empty, const uint8_t *stg, const float *xs,
                                              const float2 *xsum) {
+    constexpr int NCW = Cfg<MT>::NCW;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = a.k, U = K / 32, R = s.rows_per_stage, NS = a.ns;
     const int nst = (r1 - r0 + R - 1) / R;
     const bool pair = s.w2 != nullptr;
+    unsigned long long best[MT];
+#pragma unroll
+    for (int m = 0; m < MT; m++) best[m] = 0ull;
     for (int i = 0; i < nst; i++) {
         const int slot = i % NS;
         if (!mbar_wait(&full[slot], (uint32_t)((i / NS) & 1))) return;
@@ -110,7 +209,7 @@ __device__ __forceinline__ void gemv_consume(const GemvArgs &a, const GemvSeg &s
         const int64_t a1 = ((int64_t)rbn * s.rb + 15) & ~int64_t(15);
         const int64_t c0 = ((int64_t)ra * s.rb2) & ~int64_t(15);
         const uint8_t *buf = stg + (size_t)slot * a.stage_bytes;
-        for (int rr = warp; rr < rbn - ra; rr += 8) {
+        for (int rr = warp; rr < rbn - ra; rr += NCW) {
             const int n = ra + rr;
             const uint8_t *rp = buf + ((int64_t)n * s.rb - a0);
             float acc[MT], acc2[MT];
@@ -129,32 +228,74 @@ __device__ __forceinline__ void gemv_consume(const GemvArgs &a, const GemvSeg &s
                 acc[m] = warp_sum(acc[m]);
                 if (pair) acc2[m] = warp_sum(acc2[m]);
             }
-            if (lane == 0) {
-#pragma unroll
-                for (int m = 0; m < MT; m++) {
-                    if (m < a.m) {
-                        float v = acc[m];
-                        if (s.bias) v += s.bias[n];
-                        float *yp = s.y + (int64_t)(s.yrow ? s.yrow[m] : m) * s.ldy + n;
-                        if (s.epi == EPI_ADD) {
-                            *yp += v;
-                        } else if (s.epi == EPI_SWIGLU) {
-                            const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, fast_exp(-v)));
-                            *yp = __fmul_rn(__fmul_rn(v, sg), acc2[m]);
-                        } else {
-                            *yp = v;
-                        }
-                    }
-                }
-            }
+            if (lane == 0) row_out<MT>(s, n, a.m, acc, acc2, best);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
     }
+    flush_argmax<MT>(s, a.m, best);
 }
 
-template <int MT>
-__global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(const __grid_constant__ GemvArgs a) {
+template <int T, int MT>
+__device__ __forceinline__ void consume_wide(const GemvArgs &a, const GemvSeg &s, int r0, int r1, uint64_t *full,
+                                             uint64_t *empty, const uint8_t *stg, const float *xw,
+                                             const float *xs32) {
+    if constexpr (sb_supported<T>()) {
+        constexpr int NCW = Cfg<MT>::NCW;
+        constexpr int SB = SpanBytes<T>::v;
+        const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+        const int K = a.k, NSB = K / 256, R = s.rows_per_stage, NS = a.ns;
+        const int lpr = a.lpr, rpw = 32 / lpr, spl = NSB / lpr;
+        const int xstr = NSB * 260, sstr = K / 32;
+        const int nst = (r1 - r0 + R - 1) / R;
+        const bool pair = s.w2 != nullptr;
+        const int sub = lane % lpr;
+        unsigned long long best[MT];
+#pragma unroll
+        for (int m = 0; m < MT; m++) best[m] = 0ull;
+        for (int i = 0; i < nst; i++) {
+            const int slot = i % NS;
+            if (!mbar_wait(&full[slot], (uint32_t)((i / NS) & 1))) return;
+            const int ra = r0 + i * R, rbn = min(ra + R, r1);
+            const int64_t a0 = ((int64_t)ra * s.rb) & ~int64_t(15);
+            const int64_t a1 = ((int64_t)rbn * s.rb + 15) & ~int64_t(15);
+            const int64_t c0 = ((int64_t)ra * s.rb2) & ~int64_t(15);
+            const uint8_t *buf = stg + (size_t)slot * a.stage_bytes;
+            for (int gb = warp * rpw; gb < rbn - ra; gb += NCW * rpw) {
+                const int rr = gb + lane / lpr;
+                const bool valid = rr < rbn - ra;
+                const int n = ra + rr;
+                float acc[MT], acc2[MT];
+#pragma unroll
+                for (int m = 0; m < MT; m++) acc[m] = acc2[m] = 0.f;
+                if (valid) {
+                    const uint8_t *rp = buf + ((int64_t)n * s.rb - a0);
+                    const uint8_t *rp2 = pair ? buf + (a1 - a0) + ((int64_t)n * s.rb2 - c0) : nullptr;
+                    for (int j = 0; j < spl; j++) {
+                        const int sb = sub + j * lpr;
+                        sb_dot<T, MT>(rp + (int64_t)sb * SB, xw + sb * 260, xstr, xs32 + sb * 8, sstr, a.m, acc);
+                        if (pair)
+                            sb_dot<T, MT>(rp2 + (int64_t)sb * SB, xw + sb * 260, xstr, xs32 + sb * 8, sstr, a.m, acc2);
+                    }
+                }
+#pragma unroll
+                for (int m = 0; m < MT; m++)
+                    for (int o = lpr >> 1; o > 0; o >>= 1) {
+                        acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+                        if (pair) acc2[m] += __shfl_xor_sync(0xffffffffu, acc2[m], o);
+                    }
+                if (valid && sub == 0) row_out<MT>(s, n, a.m, acc, acc2, best);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        flush_argmax<MT>(s, a.m, best);
+    }
+}
+
+template <int MT, int TA, int TB>
+__global__ void __launch_bounds__(Cfg<MT>::NT, 1) k_gemv(const __grid_constant__ GemvArgs a) {
+    constexpr int NCW = Cfg<MT>::NCW;
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5;
     int sid = 0;
@@ -168,25 +309,31 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(const __grid_constant_
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + GEMV_NS_MAX;
     float *xs = reinterpret_cast<float *>(smem + 128);
-    float2 *xsum = reinterpret_cast<float2 *>(xs + MT * K);
-    float *red = reinterpret_cast<float *>(xsum + MT * (K / 32));
+    float *xsum = xs + x_area_floats(K, MT, a.lpr);
+    float *red = xsum + 2 * MT * (K / 32);
     uint8_t *stg = smem + a.stage_off;
     if (tid == 0) {
         for (int i = 0; i < a.ns; i++) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 8);
+            mbar_init(&empty[i], NCW);
         }
         fence_mbar_init();
     }
     __syncthreads();
-    if (r1 <= r0) return;
+    if (tid == 0) pdl_trigger();
+    if (r1 <= r0) {
+        pdl_wait();
+        return;
+    }
     const int R = s.rows_per_stage, NS = a.ns;
     const int nst = (r1 - r0 + R - 1) / R;
-    if (warp == 8) {
+    if (warp == NCW) {
+        // producer: weights do not depend on earlier kernels -- stream them
+        // before waiting on the predecessor
         if ((tid & 31) == 0) {
             for (int i = 0; i < nst; i++) {
                 const int slot = i % NS;
-                if (i >= NS && !mbar_wait(&empty[slot], (uint32_t)(((i / NS) - 1) & 1))) return;
+                if (i >= NS && !mbar_wait(&empty[slot], (uint32_t)(((i / NS) - 1) & 1))) break;
                 const int ra = r0 + i * R, rbn = min(ra + R, r1);
                 const int64_t a0 = ((int64_t)ra * s.rb) & ~int64_t(15);
                 const int64_t a1 = ((int64_t)rbn * s.rb + 15) & ~int64_t(15);
@@ -203,61 +350,75 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_gemv(const __grid_constant_
                 if (s.w2) bulk_g2s(dst + (a1 - a0), s.w2 + c0, (uint32_t)(c1 - c0), &full[slot]);
             }
         }
+        pdl_wait();
         return;
     }
-    switch (s.type) {
-#define ACM_GEMV_CASE(T)                                              \
-    case T:                                                           \
-        prep_x<T, MT>(a, xs, xsum, red);                              \
-        gemv_consume<T, MT>(a, s, r0, r1, full, empty, stg, xs, xsum); \
-        break;
-        ACM_GEMV_CASE(T_Q4_K)
-        ACM_GEMV_CASE(T_Q6_K)
-        ACM_GEMV_CASE(T_Q8_0)
-        ACM_GEMV_CASE(T_Q5_K)
-        ACM_GEMV_CASE(T_Q4_0)
-        ACM_GEMV_CASE(T_Q5_0)
-        ACM_GEMV_CASE(T_F16)
-        ACM_GEMV_CASE(T_F32)
-#undef ACM_GEMV_CASE
-        default:
-            break;
+    pdl_wait();
+#define ACM_GEMV_BODY(T)                                                                               \
+    prep_x<T, MT>(a, xs, xsum, red);                                                                   \
+    if (a.lpr) consume_wide<T, MT>(a, s, r0, r1, full, empty, stg, xs, xsum);                          \
+    else consume_unit<T, MT>(a, s, r0, r1, full, empty, stg, xs, reinterpret_cast<const float2 *>(xsum));
+    if (s.type == TA) {
+        ACM_GEMV_BODY(TA)
+    } else if constexpr (TB != TA) {
+        if (s.type == TB) {
+            ACM_GEMV_BODY(TB)
+        }
     }
+#undef ACM_GEMV_BODY
 }
 
 static const int SMEM_MAX = 227 * 1024;
 
-static size_t x_bytes(int64_t k, int mt) {
-    size_t b = 128 + (size_t)mt * k * 4 + (size_t)mt * (k / 32) * 8 + 8 * mt * 4;
-    return (b + 127) & ~size_t(127);
-}
+static int mt_of(int m) { return m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : 8; }
 
 bool gemv_supported(int type, int64_t k, int m) {
     if (!type_ok(type) || m < 1 || m > 8 || k % 32 || k % blk_elems(type)) return false;
-    const int mt = m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : 8;
-    const size_t xb = x_bytes(k, mt);
+    const int mt = mt_of(m);
+    const size_t xb = x_bytes(k, mt, 0);
     const int64_t rb = row_bytes(type, k);
     return xb + 2 * (size_t)(2 * rb + 64 + 128) + 16 <= (size_t)SMEM_MAX;
 }
 
-template <int MT>
-static cudaError_t launch_mt(GemvArgs &a, int grid, size_t smem, cudaStream_t st) {
+static bool sb_ok(int type) {
+    return type == T_Q4_K || type == T_Q5_K || type == T_Q6_K || type == T_Q8_0 || type == T_F16;
+}
+
+template <int MT, int TA, int TB>
+static cudaError_t launch_one(GemvArgs &a, int grid, size_t smem, cudaStream_t st) {
     static bool attr_done[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr_done[dev & 63]) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemv<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX);
+        cudaError_t e = cudaFuncSetAttribute(k_gemv<MT, TA, TB>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX);
         if (e != cudaSuccess) return e;
         attr_done[dev & 63] = true;
     }
-    k_gemv<MT><<<grid, GEMV_THREADS, smem, st>>>(a);
+    cudaError_t e = launch_pdl(k_gemv<MT, TA, TB>, dim3(grid), dim3(Cfg<MT>::NT), smem, st, a);
+    if (e != cudaSuccess) return e;
     return launched(1);
 }
 
-cudaError_t gemv_launch(const GemvSegDesc *segs, int nseg, const float *x, int ldx, int64_t k, int m,
-                        const float *norm_w, float eps, int num_sms, cudaStream_t st) {
-    if (nseg < 1 || nseg > GEMV_MAX_SEG || m < 1 || m > 8) return cudaErrorInvalidValue;
-    const int mt = m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : 8;
+template <int MT>
+static cudaError_t launch_types(GemvArgs &a, int ta, int tb, int grid, size_t smem, cudaStream_t st) {
+    if (ta == T_Q4_K && tb == T_Q6_K) return launch_one<MT, T_Q4_K, T_Q6_K>(a, grid, smem, st);
+    switch (ta) {
+        case T_Q4_K: return launch_one<MT, T_Q4_K, T_Q4_K>(a, grid, smem, st);
+        case T_Q6_K: return launch_one<MT, T_Q6_K, T_Q6_K>(a, grid, smem, st);
+        case T_Q8_0: return launch_one<MT, T_Q8_0, T_Q8_0>(a, grid, smem, st);
+        case T_Q5_K: return launch_one<MT, T_Q5_K, T_Q5_K>(a, grid, smem, st);
+        case T_Q4_0: return launch_one<MT, T_Q4_0, T_Q4_0>(a, grid, smem, st);
+        case T_Q5_0: return launch_one<MT, T_Q5_0, T_Q5_0>(a, grid, smem, st);
+        case T_F16: return launch_one<MT, T_F16, T_F16>(a, grid, smem, st);
+        case T_F32: return launch_one<MT, T_F32, T_F32>(a, grid, smem, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+// One launch for segments whose types are {ta} or {ta, tb}.
+static cudaError_t gemv_launch_group(const GemvSegDesc *segs, int nseg, int ta, int tb, const float *x, int ldx,
+                                     int64_t k, int m, const float *norm_w, float eps, int num_sms, cudaStream_t st) {
+    const int mt = mt_of(m);
     GemvArgs a{};
     a.nseg = nseg;
     a.x = x;
@@ -266,8 +427,6 @@ cudaError_t gemv_launch(const GemvSegDesc *segs, int nseg, const float *x, int l
     a.m = m;
     a.norm_w = norm_w;
     a.eps = eps;
-    const size_t xb = x_bytes(k, mt);
-    // stage size: 32 KB target, at least two rows (pair: both matrices)
     int64_t maxrow = 0;
     double total_bytes = 0;
     for (int i = 0; i < nseg; i++) {
@@ -275,19 +434,53 @@ cudaError_t gemv_launch(const GemvSegDesc *segs, int nseg, const float *x, int l
         maxrow = std::max(maxrow, rb);
         total_bytes += (double)rb * (double)segs[i].n;
     }
+    // wide path: a single large matrix whose format has a span decoder
+    a.lpr = 0;
+    if (nseg == 1 && sb_ok(segs[0].type) && k % 256 == 0 && segs[0].n / num_sms >= 128) {
+        const int nsb = (int)(k / 256);
+        int lpr = 1;
+        while (lpr * 2 <= 4 && nsb % (lpr * 2) == 0) lpr *= 2;
+        a.lpr = lpr;
+    }
+    const size_t xb = x_bytes(k, mt, a.lpr);
     // a stage holds R rows plus up to 60 bytes of 16-byte rounding (two
     // copies) and the 4-byte over-read of the unaligned word loader
     int64_t sb = std::max<int64_t>(32 * 1024, ((maxrow + 64 + 127) / 128) * 128);
+    if (a.lpr) {
+        // enough rows per stage for every consumer warp to take a row group
+        const int ncw = mt <= 2 ? 16 : 8;
+        sb = std::max<int64_t>(sb, (((int64_t)ncw * (32 / a.lpr) * maxrow + 64 + 127) / 128) * 128);
+    }
     int ns = (int)std::min<int64_t>(6, ((int64_t)SMEM_MAX - (int64_t)xb - 16) / sb);
     if (ns < 2) {
         sb = ((maxrow + 64 + 127) / 128) * 128;
         ns = (int)std::min<int64_t>(GEMV_NS_MAX, ((int64_t)SMEM_MAX - (int64_t)xb - 16) / sb);
         if (ns < 2) return cudaErrorInvalidValue;
     }
+    // small matrices: shrink the ring to the stages a CTA actually needs, so
+    // the kernel's shared memory leaves room for the next kernel's CTAs to
+    // start early (programmatic dependent launch) and prefetch their weights
+    {
+        int64_t need_stages = 1, need_bytes = 0;
+        for (int i = 0; i < nseg; i++) {
+            const int64_t rbp = row_bytes(segs[i].type, k) * (segs[i].w2 ? 2 : 1);
+            const double share = (double)rbp * (double)segs[i].n / total_bytes;
+            const int nc = std::max(1, std::min<int>((int)(share * num_sms + 0.5), (int)segs[i].n));
+            const int64_t rows = (segs[i].n + nc - 1) / nc;
+            const int64_t rps = (sb - 64) / rbp;
+            need_stages = std::max<int64_t>(need_stages, (rows + rps - 1) / std::max<int64_t>(rps, 1));
+            need_bytes = std::max<int64_t>(need_bytes, rows * rbp + 64);
+        }
+        if (need_stages == 1) {
+            sb = std::min<int64_t>(sb, ((need_bytes + 127) / 128) * 128);
+            ns = 1;
+        } else {
+            ns = (int)std::min<int64_t>(ns, need_stages);
+        }
+    }
     a.ns = ns;
     a.stage_bytes = (int)sb;
     a.stage_off = (int)xb;
-    // CTAs per segment proportional to its bytes
     int grid = 0;
     for (int i = 0; i < nseg; i++) {
         GemvSeg &g = a.seg[i];
@@ -303,6 +496,7 @@ cudaError_t gemv_launch(const GemvSegDesc *segs, int nseg, const float *x, int l
         g.ldy = d.ldy;
         g.bias = d.bias;
         g.yrow = d.yrow;
+        g.amax = d.amax;
         const double share = (double)(g.rb + g.rb2) * (double)d.n / total_bytes;
         int nc = (int)(share * num_sms + 0.5);
         nc = std::max(1, std::min<int>(nc, (int)d.n));
@@ -314,11 +508,44 @@ cudaError_t gemv_launch(const GemvSegDesc *segs, int nseg, const float *x, int l
     }
     const size_t smem = xb + (size_t)ns * (size_t)sb + 16;
     switch (mt) {
-        case 1: return launch_mt<1>(a, grid, smem, st);
-        case 2: return launch_mt<2>(a, grid, smem, st);
-        case 4: return launch_mt<4>(a, grid, smem, st);
-        default: return launch_mt<8>(a, grid, smem, st);
+        case 1: return launch_types<1>(a, ta, tb, grid, smem, st);
+        case 2: return launch_types<2>(a, ta, tb, grid, smem, st);
+        case 4: return launch_types<4>(a, ta, tb, grid, smem, st);
+        default: return launch_types<8>(a, ta, tb, grid, smem, st);
     }
+}
+
+cudaError_t gemv_launch(const GemvSegDesc *segs, int nseg, const float *x, int ldx, int64_t k, int m,
+                        const float *norm_w, float eps, int num_sms, cudaStream_t st) {
+    if (nseg < 1 || nseg > GEMV_MAX_SEG || m < 1 || m > 8) return cudaErrorInvalidValue;
+    // common instance: every type equal, or exactly {Q4_K, Q6_K}
+    bool same = true, q46 = true;
+    for (int i = 0; i < nseg; i++) {
+        same &= segs[i].type == segs[0].type;
+        q46 &= segs[i].type == T_Q4_K || segs[i].type == T_Q6_K;
+    }
+    if (same) return gemv_launch_group(segs, nseg, segs[0].type, segs[0].type, x, ldx, k, m, norm_w, eps, num_sms, st);
+    if (q46) return gemv_launch_group(segs, nseg, T_Q4_K, T_Q6_K, x, ldx, k, m, norm_w, eps, num_sms, st);
+    // otherwise one launch per distinct type (CTAs split by bytes)
+    double tot = 0;
+    for (int j = 0; j < nseg; j++) tot += (double)row_bytes(segs[j].type, k) * segs[j].n;
+    for (int i = 0; i < nseg; i++) {
+        bool first = true;
+        for (int j = 0; j < i; j++) first &= segs[j].type != segs[i].type;
+        if (!first) continue;
+        std::vector<GemvSegDesc> grp;
+        double frac = 0;
+        for (int j = i; j < nseg; j++)
+            if (segs[j].type == segs[i].type) {
+                grp.push_back(segs[j]);
+                frac += (double)row_bytes(segs[j].type, k) * segs[j].n;
+            }
+        const int sms = std::max(1, (int)(num_sms * frac / tot + 0.5));
+        cudaError_t e = gemv_launch_group(grp.data(), (int)grp.size(), segs[i].type, segs[i].type, x, ldx, k, m,
+                                          norm_w, eps, sms, st);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 int read_and_clear_dev_error() {

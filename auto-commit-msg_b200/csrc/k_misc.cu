@@ -7,6 +7,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 #include "quant.cuh"
 
 namespace acm {
@@ -18,6 +19,8 @@ namespace acm {
 template <int T>
 __global__ void __launch_bounds__(256) k_dequant(const uint8_t *w, int64_t rb, int64_t K, int64_t nrows,
                                                  const int32_t *ids, int64_t src_rows, float *out, int64_t ldo) {
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
     const int64_t runs = K / 32, total = nrows * runs;
     for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
          idx += (int64_t)gridDim.x * blockDim.x) {
@@ -49,7 +52,7 @@ cudaError_t dequant_launch(int type, const void *w, int64_t k, int64_t nrows, co
     const int64_t rb = row_bytes(type, k);
     switch (type) {
 #define ACM_DQ(T) \
-    case T: k_dequant<T><<<grid, 256, 0, st>>>(wb, rb, k, nrows, row_ids, src_rows, out, ldo); break;
+    case T: launch_pdl(k_dequant<T>, dim3(grid), dim3(256), 0, st, wb, rb, k, nrows, row_ids, src_rows, out, ldo); break;
         ACM_DQ(T_F32) ACM_DQ(T_F16) ACM_DQ(T_Q4_0) ACM_DQ(T_Q5_0) ACM_DQ(T_Q8_0) ACM_DQ(T_Q4_K) ACM_DQ(T_Q5_K)
         ACM_DQ(T_Q6_K)
 #undef ACM_DQ
@@ -62,6 +65,8 @@ cudaError_t dequant_launch(int type, const void *w, int64_t k, int64_t nrows, co
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_rmsnorm(const float *x, int ldx, const float *w, float *y, int ldy, int n,
                                                  float eps) {
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
     __shared__ float red[8];
     const float *xr = x + (int64_t)blockIdx.x * ldx;
     float *yr = y + (int64_t)blockIdx.x * ldy;
@@ -80,7 +85,7 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const float *x, int ldx, const 
 cudaError_t rmsnorm_launch(const float *x, int ldx, const float *w, float *y, int ldy, int m, int n, float eps,
                            cudaStream_t st) {
     if (m <= 0) return cudaSuccess;
-    k_rmsnorm<<<m, 256, 0, st>>>(x, ldx, w, y, ldy, n, eps);
+    launch_pdl(k_rmsnorm, dim3(m), dim3(256), 0, st, x, ldx, w, y, ldy, n, eps);
     return launched(1);
 }
 
@@ -96,6 +101,8 @@ __device__ __forceinline__ int64_t kv_off(const KVDesc &kv, int layer, int seq, 
 }
 
 __global__ void __launch_bounds__(256) k_rope_append(const RopeDesc r, const KVDesc kv, int layer, TokMeta tm) {
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
     extern __shared__ float sh[];  // 8 warps x head_dim
     const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int hh = blockIdx.y * 8 + warp;
@@ -149,7 +156,7 @@ cudaError_t rope_append_launch(const RopeDesc &r, const KVDesc &kv, int layer, T
                                cudaStream_t st) {
     if (ntok <= 0) return cudaSuccess;
     dim3 grid(ntok, (r.n_head + r.n_head_kv + 7) / 8);
-    k_rope_append<<<grid, 256, 8 * r.head_dim * sizeof(float), st>>>(r, kv, layer, tm);
+    launch_pdl(k_rope_append, grid, dim3(256), 8 * r.head_dim * sizeof(float), st, r, kv, layer, tm);
     return launched(1);
 }
 
@@ -160,19 +167,6 @@ cudaError_t rope_append_launch(const RopeDesc &r, const KVDesc &kv, int layer, T
 // the order of greedy() and topK() (sampler.go:19-27, :80-98).  NaN logits
 // rank last (the reference's comparisons never select them).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint64_t logit_key(float v, int idx) {
-    uint32_t b = __float_as_uint(v);
-    uint32_t o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-    if (v != v) o = 0;
-    return ((uint64_t)o << 32) | (uint32_t)(0xFFFFFFFFu - (uint32_t)idx);
-}
-__device__ __forceinline__ float key_logit(uint64_t k) {
-    uint32_t o = (uint32_t)(k >> 32);
-    uint32_t b = (o & 0x80000000u) ? (o & 0x7FFFFFFFu) : ~o;
-    return __uint_as_float(b);
-}
-__device__ __forceinline__ int key_index(uint64_t k) { return (int)(0xFFFFFFFFu - (uint32_t)k); }
-
 constexpr int SAMPLE_CHUNK = 2048;
 constexpr int TOPK_MAX = 64;
 
@@ -199,6 +193,8 @@ __device__ void bitonic_desc(uint64_t *s, int n) {
 // Per chunk of SAMPLE_CHUNK logits: the top `kk` keys (kk = 1 or 64).
 __global__ void __launch_bounds__(256) k_topk_partial(const float *logits, const int32_t *rows, int64_t ld,
                                                       int vocab, int kk, uint64_t *cand, int nchunks) {
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
     __shared__ uint64_t s[SAMPLE_CHUNK];
     const int t = blockIdx.y, c = blockIdx.x;
     const float *lg = logits + (int64_t)(rows ? rows[t] : t) * ld;
@@ -256,6 +252,8 @@ __device__ __forceinline__ double philox_uniform(uint64_t seed, uint64_t step) {
 // Merge the per-chunk candidates of one token and draw (Sample,
 // sampler.go:30-76; the fp64 part runs on one thread in the reference's order).
 __global__ void __launch_bounds__(1024) k_sample_final(SampleDesc d, int kk) {
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
     extern __shared__ uint64_t s[];
     const int t = blockIdx.x;
     const int n = d.nchunks * kk;
@@ -315,7 +313,7 @@ cudaError_t sample_launch(const SampleDesc &d, int ntok, bool all_greedy, cudaSt
     if (ntok <= 0) return cudaSuccess;
     const int kk = all_greedy ? 1 : TOPK_MAX;
     dim3 g1(d.nchunks, ntok);
-    k_topk_partial<<<g1, 256, 0, st>>>(d.logits, d.rows, d.ld, d.vocab, kk, d.cand, d.nchunks);
+    launch_pdl(k_topk_partial, g1, dim3(256), 0, st, d.logits, d.rows, d.ld, d.vocab, kk, d.cand, d.nchunks);
     int np = 1;
     while (np < d.nchunks * kk) np <<= 1;
     const size_t smem = (size_t)np * sizeof(uint64_t);
@@ -327,12 +325,14 @@ cudaError_t sample_launch(const SampleDesc &d, int ntok, bool all_greedy, cudaSt
         attr[dev & 63] = true;
     }
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
-    k_sample_final<<<ntok, 1024, smem, st>>>(d, kk);
+    launch_pdl(k_sample_final, dim3(ntok), dim3(1024), smem, st, d, kk);
     return launched(2);
 }
 
 // ---------------------------------------------------------------------------
 __global__ void k_swiglu(const float *g, const float *u, float *y, int64_t n) {
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const float v = g[i];
         const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, fast_exp(-v)));
@@ -342,28 +342,40 @@ __global__ void k_swiglu(const float *g, const float *u, float *y, int64_t n) {
 
 cudaError_t swiglu_launch(const float *g, const float *u, float *y, int64_t n, cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
-    k_swiglu<<<(int)std::min<int64_t>((n + 255) / 256, 148 * 8), 256, 0, st>>>(g, u, y, n);
+    launch_pdl(k_swiglu, dim3((unsigned)std::min<int64_t>((n + 255) / 256, 148 * 8)), dim3(256), 0, st, g, u, y, n);
     return launched(1);
 }
 
-__global__ void k_advance(int32_t *tok, int32_t *pos, uint64_t *step, const int32_t *out, int32_t *hist,
-                          int hist_ld, int32_t *hist_col, int ntok) {
+__global__ void k_advance(int32_t *tok, int32_t *pos, uint64_t *step, int32_t *out, unsigned long long *amax,
+                          int32_t *hist, int hist_ld, int32_t *hist_col, int ntok) {
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
     const int t = threadIdx.x;
     if (t < ntok) {
         const int col = *hist_col;
-        tok[t] = out[t];
+        int32_t id;
+        if (amax) {  // greedy: the lm_head epilogue folded every row into amax[t]
+            id = key_index(amax[t]);
+            amax[t] = 0ull;
+            out[t] = id;
+        } else {
+            id = out[t];
+        }
+        tok[t] = id;
         pos[t] += 1;
         step[t] += 1;
-        if (hist && col >= 0 && col < hist_ld) hist[(int64_t)t * hist_ld + col] = out[t];
+        if (hist && col >= 0 && col < hist_ld) hist[(int64_t)t * hist_ld + col] = id;
     }
     __syncthreads();
     if (t == 0) *hist_col += 1;
 }
 
-cudaError_t advance_launch(int32_t *tok, int32_t *pos, uint64_t *step, const int32_t *out, int32_t *hist,
-                           int hist_ld, int32_t *hist_col, int ntok, cudaStream_t st) {
+cudaError_t advance_launch(int32_t *tok, int32_t *pos, uint64_t *step, int32_t *out, unsigned long long *amax,
+                           int32_t *hist, int hist_ld, int32_t *hist_col, int ntok, cudaStream_t st) {
     if (ntok <= 0 || ntok > 1024) return cudaErrorInvalidValue;
-    k_advance<<<1, ((ntok + 31) / 32) * 32, 0, st>>>(tok, pos, step, out, hist, hist_ld, hist_col, ntok);
+    cudaError_t e = launch_pdl(k_advance, dim3(1), dim3(((ntok + 31) / 32) * 32), 0, st, tok, pos, step, out, amax,
+                               hist, hist_ld, hist_col, ntok);
+    if (e != cudaSuccess) return e;
     return launched(1);
 }
 

@@ -10,6 +10,9 @@ namespace acm {
 // Device error flag values (set by kernels, read by the host after a sync).
 enum : int { DEV_ERR_NONE = 0, DEV_ERR_TIMEOUT = 1, DEV_ERR_BOUNDS = 2 };
 
+// Programmatic dependent launch on the decode path (env ACM_PDL=0 disables).
+extern bool g_pdl;
+
 // Epilogues shared by the GEMV and GEMM kernels.
 enum : int {
     EPI_STORE = 0,   // y = W x (+ bias)
@@ -30,10 +33,10 @@ struct GemvSeg {
     int ldy;
     const float *bias;      // optional, n floats
     const int32_t *yrow;    // optional: output row of token m (default m)
+    unsigned long long *amax;  // optional: per-token running argmax key (greedy sampling)
 };
 
 constexpr int GEMV_MAX_SEG = 4;
-constexpr int GEMV_THREADS = 288;  // 8 consumer warps + 1 producer warp
 constexpr int GEMV_NS_MAX = 8;
 
 struct GemvArgs {
@@ -48,9 +51,9 @@ struct GemvArgs {
     int ns;              // pipeline stages
     int stage_bytes;
     int stage_off;       // byte offset of the stage ring in shared memory
+    int lpr;             // 0: one row per warp (unit path); else lanes per row (wide path)
 };
 
-// Plans CTA ranges / stages and launches.  Returns a cudaError_t.
 struct GemvSegDesc {
     const void *w, *w2;
     int type;
@@ -60,7 +63,10 @@ struct GemvSegDesc {
     int ldy;
     const float *bias;
     const int32_t *yrow;
+    unsigned long long *amax;
 };
+// Plans CTA ranges / stages and launches (possibly several launches when the
+// segments' types have no common kernel instance).  Returns a cudaError_t.
 cudaError_t gemv_launch(const GemvSegDesc *segs, int nseg, const float *x, int ldx, int64_t k, int m,
                         const float *norm_w, float eps, int num_sms, cudaStream_t st);
 bool gemv_supported(int type, int64_t k, int m);
@@ -127,9 +133,15 @@ struct AttnDesc {
     float scale;
     float *part;      // split partials [ntok][n_head][nsplit][head_dim + 2]
     int nsplit;
+    int *counter;     // [ntok][n_head_kv] split-arrival counters (decode kernel)
 };
 cudaError_t attention_launch(const AttnDesc &a, const KVDesc &kv, int layer, TokMeta tm, int ntok, int max_pos,
                              cudaStream_t st);
+// Decode attention for a batch of tokens of distinct sequences with the
+// QK-norm / RoPE / KV append of the new token fused in, and the split merge
+// done by the last split of each (token, kv head).
+cudaError_t attention_decode_launch(const RopeDesc &r, const AttnDesc &a, const KVDesc &kv, int layer, TokMeta tm,
+                                    int ntok, int max_pos, cudaStream_t st);
 
 // y = silu(g) * u elementwise (fallback when gate and up differ in type).
 cudaError_t swiglu_launch(const float *g, const float *u, float *y, int64_t n, cudaStream_t st);
@@ -151,10 +163,11 @@ struct SampleDesc {
 };
 cudaError_t sample_launch(const SampleDesc &s, int ntok, bool all_greedy, cudaStream_t st);
 
-// After a decode step: next input = sampled id, position + 1, step + 1, and
-// the id recorded in hist[t][hist_col] (device-side token loop).
-cudaError_t advance_launch(int32_t *tok, int32_t *pos, uint64_t *step, const int32_t *out, int32_t *hist,
-                           int hist_ld, int32_t *hist_col, int ntok, cudaStream_t st);
+// After a decode step: next input = sampled id (or, when amax is given, the
+// argmax the lm_head epilogue accumulated, which is then cleared), position
+// + 1, step + 1, and the id recorded in hist[t][hist_col].
+cudaError_t advance_launch(int32_t *tok, int32_t *pos, uint64_t *step, int32_t *out, unsigned long long *amax,
+                           int32_t *hist, int hist_ld, int32_t *hist_col, int ntok, cudaStream_t st);
 
 // Device error flag (timeouts in bounded waits).
 int read_and_clear_dev_error();
