@@ -13,17 +13,13 @@
 // (sum e*v, max, sum e) triples.
 #include <float.h>
 
+#include "attn_dev.cuh"
 #include "common.cuh"
 #include "kernels.h"
 #include "launch.cuh"
 #include "quant.cuh"
 
 namespace acm {
-
-__device__ __forceinline__ const float *kv_row(const float *pool, const KVDesc &kv, int layer, int seq, int pos) {
-    const int page = kv.page_table[(int64_t)seq * kv.max_pages + (pos / kv.page_size)];
-    return pool + (int64_t)layer * kv.layer_stride + ((int64_t)page * kv.page_size + (pos % kv.page_size)) * kv.kvd;
-}
 
 template <int HD>
 __global__ void __launch_bounds__(128) k_attn(const AttnDesc a, const KVDesc kv, int layer, TokMeta tm,
@@ -171,31 +167,6 @@ __global__ void k_attn_combine(const AttnDesc a) {
 // it writes (sum e*v, max, sum e) and the last CTA to arrive merges.
 // ---------------------------------------------------------------------------
 constexpr int ATT_CHUNK = 32;
-
-template <int HD>
-__device__ __forceinline__ void head_norm_rope(float *v, const float *nw, const RopeDesc &r, int pos, int lane) {
-    // v: HD floats in shared memory (one warp); rmsnorm (model.go:213-222)
-    // then rope (model.go:237-251) in place
-    if (nw) {
-        float ss = 0.f;
-        for (int d = lane; d < HD; d += 32) ss = fmaf(v[d], v[d], ss);
-        ss = warp_sum(ss);
-        const float sc = rms_scale(ss, HD, r.eps);
-        __syncwarp();
-        for (int d = lane; d < HD; d += 32) v[d] = __fmul_rn(__fmul_rn(v[d], sc), nw[d]);
-    }
-    __syncwarp();
-    const int half = r.rope_dim / 2;
-    const float2 *tab = r.tab + (int64_t)pos * half;
-    for (int i = lane; i < half; i += 32) {
-        const int ia = r.interleaved ? 2 * i : i, ib = r.interleaved ? 2 * i + 1 : i + half;
-        const float a = v[ia], b = v[ib];
-        const float2 cs = tab[i];
-        v[ia] = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
-        v[ib] = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
-    }
-    __syncwarp();
-}
 
 template <int HD>
 __global__ void __launch_bounds__(128) k_attn_decode(const RopeDesc r, const AttnDesc a, const KVDesc kv, int layer,
@@ -370,6 +341,184 @@ cudaError_t attention_decode_launch(const RopeDesc &r, const AttnDesc &a, const 
     dim3 grid(ntok, a.n_head_kv, nchunk);
     cudaError_t e = HD == 128 ? launch_pdl(k_attn_decode<128>, grid, dim3(128), smem, st, r, a, kv, layer, tm)
                               : launch_pdl(k_attn_decode<64>, grid, dim3(128), smem, st, r, a, kv, layer, tm);
+    if (e != cudaSuccess) return e;
+    return launched(1);
+}
+
+// ---------------------------------------------------------------------------
+// Prefill attention: the tokens of the batch are consecutive positions of one
+// sequence (keys/values already appended).  CTA (tile, g): QT query tokens x
+// the G query heads of kv head g = R = QT*G rows.  Two passes over 32-position
+// key tiles staged in shared memory: pass 1 finds each row's maximum score,
+// pass 2 forms e = fastExp(s - max) exactly as the reference's softmax
+// (model.go:297-313) and accumulates e*v and sum e; out = sum(e*v) / sum(e).
+// Scores and P.V are register-tiled FFMA (4 rows x 4 keys, 8 rows x 8 dims).
+// ---------------------------------------------------------------------------
+constexpr int PQT = 16;  // query tokens per CTA
+constexpr int PKT = 32;  // keys per tile
+
+template <int HD>
+__global__ void __launch_bounds__(256) k_attn_prefill(const AttnDesc a, const KVDesc kv, int layer, TokMeta tm,
+                                                      int ntok) {
+    extern __shared__ __align__(16) float psm[];
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
+    const int G = a.n_head / a.n_head_kv, nh = a.n_head, qd = nh * HD;
+    const int tile = blockIdx.x, g = blockIdx.y, tid = threadIdx.x;
+    const int t0 = tile * PQT, nt = min(PQT, ntok - t0);
+    const int R = PQT * G;  // rows (token-major: r = tq*G + h)
+    const int seq = tm.seq[t0], pos0 = tm.pos[t0];
+    const int max_pos = pos0 + nt - 1;
+    constexpr int QS = HD + 4;  // padded row strides
+    float *qs = psm;                     // [R][QS]
+    float *ks = qs + R * QS;             // [PKT][QS]
+    float *vs = ks + PKT * QS;           // [PKT][HD]
+    float *ss = vs + PKT * HD;           // [R][PKT + 1]
+    float *rmax = ss + R * (PKT + 1);    // [R]
+    float *rsum = rmax + R;              // [R]
+    for (int i = tid; i < R * HD; i += 256) {
+        const int r = i / HD, d = i - r * HD, tq = r / G, h = r - tq * G;
+        qs[r * QS + d] = tq < nt ? a.q[(int64_t)(t0 + tq) * qd + (int64_t)(g * G + h) * HD + d] : 0.f;
+    }
+    for (int r = tid; r < R; r += 256) {
+        rmax[r] = -FLT_MAX;
+        rsum[r] = 0.f;
+    }
+    const int nkt = (max_pos + PKT) / PKT;  // key tiles covering [0, max_pos]
+    // thread tiles: scores 4 rows x 4 keys (R <= 128 rows, 32 keys -> <= 256 threads)
+    const int sr = (tid / 8) * 4, sk = (tid % 8) * 4;
+    // P.V: 8 rows x 8 dims per thread over R x HD
+    const int prow = (tid / (HD / 8)) * 8, pdim = (tid % (HD / 8)) * 8;
+    float o[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) o[i][j] = 0.f;
+    for (int pass = 0; pass < 2; pass++) {
+        for (int kt = 0; kt < nkt; kt++) {
+            const int k0 = kt * PKT, kn = min(PKT, max_pos + 1 - k0);
+            __syncthreads();
+            // stage keys (and values in pass 2); a tile lies in one page
+            const int64_t base = (int64_t)layer * kv.layer_stride +
+                                 ((int64_t)kv.page_table[(int64_t)seq * kv.max_pages + k0 / kv.page_size] * kv.page_size +
+                                  (k0 % kv.page_size)) * kv.kvd + g * HD;
+            const int pieces = kn * (HD / 4);
+            for (int i = tid; i < pieces * (pass + 1); i += 256) {
+                const int which = i / pieces, rem = i - which * pieces;
+                const int p = rem / (HD / 4), c = rem - p * (HD / 4);
+                const float *src = (which ? kv.v : kv.k) + base + (int64_t)p * kv.kvd + c * 4;
+                cp_async16(which ? vs + p * HD + c * 4 : ks + p * QS + c * 4, src);
+            }
+            cp_async_wait_all();
+            __syncthreads();
+            // scores for rows sr..sr+3, keys sk..sk+3
+            if (sr < R) {
+                float acc[4][4];
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+#pragma unroll
+                    for (int j = 0; j < 4; j++) acc[i][j] = 0.f;
+                for (int d = 0; d < HD; d += 4) {
+                    float4 qv[4], kv4[4];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) qv[i] = *reinterpret_cast<const float4 *>(qs + (sr + i) * QS + d);
+#pragma unroll
+                    for (int j = 0; j < 4; j++) kv4[j] = *reinterpret_cast<const float4 *>(ks + (sk + j) * QS + d);
+#pragma unroll
+                    for (int i = 0; i < 4; i++)
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            acc[i][j] = fmaf(qv[i].x, kv4[j].x, acc[i][j]);
+                            acc[i][j] = fmaf(qv[i].y, kv4[j].y, acc[i][j]);
+                            acc[i][j] = fmaf(qv[i].z, kv4[j].z, acc[i][j]);
+                            acc[i][j] = fmaf(qv[i].w, kv4[j].w, acc[i][j]);
+                        }
+                }
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int r = sr + i, tq = r / G;
+                    const int qpos = pos0 + tq;
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const int kp = k0 + sk + j;
+                        const bool ok = sk + j < kn && kp <= qpos && tq < nt;
+                        ss[r * (PKT + 1) + sk + j] = ok ? __fmul_rn(acc[i][j], a.scale) : -FLT_MAX;
+                    }
+                }
+            }
+            __syncthreads();
+            if (pass == 0) {
+                // running row maxima
+                for (int r = tid; r < R; r += 256) {
+                    float m = rmax[r];
+                    for (int j = 0; j < kn; j++) m = fmaxf(m, ss[r * (PKT + 1) + j]);
+                    rmax[r] = m;
+                }
+            } else {
+                // e = fastExp(s - max) in place, row sums
+                for (int r = tid; r < R; r += 256) {
+                    const float m = rmax[r];
+                    float s = rsum[r];
+                    for (int j = 0; j < kn; j++) {
+                        float *e = ss + r * (PKT + 1) + j;
+                        const float v = *e == -FLT_MAX ? 0.f : fast_exp(__fsub_rn(*e, m));
+                        *e = v;
+                        s += v;
+                    }
+                    rsum[r] = s;
+                }
+                __syncthreads();
+                if (prow < R) {
+                    for (int j = 0; j < kn; j++) {
+                        const float4 v0 = *reinterpret_cast<const float4 *>(vs + j * HD + pdim);
+                        const float4 v1 = *reinterpret_cast<const float4 *>(vs + j * HD + pdim + 4);
+                        const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            const float p = ss[(prow + i) * (PKT + 1) + j];
+#pragma unroll
+                            for (int dd = 0; dd < 8; dd++) o[i][dd] = fmaf(p, vv[dd], o[i][dd]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (prow < R) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int r = prow + i, tq = r / G, h = r - tq * G;
+            if (tq >= nt) continue;
+            const float inv = rsum[r];
+            float *dst = a.out + (int64_t)(t0 + tq) * qd + (int64_t)(g * G + h) * HD + pdim;
+#pragma unroll
+            for (int dd = 0; dd < 8; dd++) dst[dd] = __fdiv_rn(o[i][dd], inv);
+        }
+    }
+}
+
+cudaError_t attention_prefill_launch(const AttnDesc &a, const KVDesc &kv, int layer, TokMeta tm, int ntok,
+                                     cudaStream_t st) {
+    if (ntok <= 0) return cudaSuccess;
+    const int G = a.n_head / a.n_head_kv, HD = a.head_dim;
+    if (G > 8 || a.n_head % a.n_head_kv || (HD != 64 && HD != 128) || kv.page_size % PKT) return cudaErrorInvalidValue;
+    const int R = PQT * G;
+    if ((R / 4) * 8 > 256 && R > 128) return cudaErrorInvalidValue;
+    const int QS = HD + 4;
+    const size_t smem = ((size_t)R * QS + PKT * QS + PKT * HD + (size_t)R * (PKT + 1) + 2 * R) * sizeof(float);
+    static bool attr[64][2] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int hi = HD == 128 ? 0 : 1;
+    if (!attr[dev & 63][hi]) {
+        cudaFuncSetAttribute(HD == 128 ? k_attn_prefill<128> : k_attn_prefill<64>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr[dev & 63][hi] = true;
+    }
+    dim3 grid((ntok + PQT - 1) / PQT, a.n_head_kv);
+    cudaError_t e = HD == 128 ? launch_pdl(k_attn_prefill<128>, grid, dim3(256), smem, st, a, kv, layer, tm, ntok)
+                              : launch_pdl(k_attn_prefill<64>, grid, dim3(256), smem, st, a, kv, layer, tm, ntok);
     if (e != cudaSuccess) return e;
     return launched(1);
 }

@@ -192,6 +192,15 @@ ACM_API int acm_model_last_timing(acm_model *m, double *prefill_s, double *decod
  * replay counts every kernel the graph holds).  No reference counterpart. */
 ACM_API uint64_t acm_kernel_launches(void);
 
+/* Tracing, no reference counterpart (the reference's only tracing is its
+ * Stats wall clock, sampler.go:101-106): when enabled, batch-1 decode steps
+ * on the persistent decode kernel record, per CTA and phase (q/k/v,
+ * attention, o, gate/up, down per layer, then lm_head), the %globaltimer ns at
+ * which the CTA started the phase and arrived at the following barrier.
+ * acm_model_trace_read copies the last step's [nblocks][nphases][2] values. */
+ACM_API int acm_model_trace(acm_model *m, int32_t enable);
+ACM_API int acm_model_trace_read(acm_model *m, uint64_t *out, int64_t cap, int32_t *nblocks, int32_t *nphases);
+
 /* Measurement helper, no reference counterpart: replay the fused
  * dequant-GEMV launches of one batch-1 decode token on this model's weights
  * (q/k/v, o, gate/up, down of every layer, then lm_head -- the matvec calls of

@@ -85,31 +85,35 @@ def test_forward_sample_topk(acm, eng, oracle, synth, tiny_models, name):
     m.close()
 
 
+def reachable(oracle, lg, temp, top_k, top_p, u, eps=3e-5, trials=64, seed=0):
+    """Ids the reference sampler can return on logits within +-eps of lg
+    (fp32 noise of a different summation order)."""
+    rng = np.random.default_rng(seed)
+    out = {oracle.sample(lg, temp, top_k, top_p, u)}
+    for _ in range(trials):
+        j = (lg + rng.uniform(-eps, eps, lg.shape)).astype(np.float32)
+        out.add(oracle.sample(j, temp, top_k, top_p, u))
+    return out
+
+
 @pytest.mark.parametrize("name", ["qwen3", "llama_q5"])
 def test_generate_topk_matches_oracle(acm, eng, oracle, synth, tiny_models, name):
     """Device-side loop (acm_generate) with top-k sampling: ids equal the
-    oracle's up to the first order tie; at that step the device's choice is
-    the reference sampler's choice on the device's logits (replayed)."""
+    oracle's up to the first step where the oracle's own choice is not
+    unique under fp32 noise of the logits (an order tie); that step's device
+    choice must be one the reference sampler reaches within that noise."""
     m = acm.Load(tiny_models[name], 0, engine=eng)
     o = oracle.Model(tiny_models[name], 0)
     p = synth.prompt_ids(20, m.Cfg.vocab, 11)
     s = acm.Sampler(0.7, 40, 0.0, Seed=77)
     got = m.Generate(p, s, 30, stop_on_eos=False)
-    want = o.generate(p, temp=0.7, top_k=40, seed=77, max_tok=30, stop_on_eos=False)["ids"].tolist()
+    r = o.generate(p, temp=0.7, top_k=40, seed=77, max_tok=30, stop_on_eos=False, keep_logits=True)
+    want = r["ids"].tolist()
+    m.close()
     j = next((i for i, (a, b) in enumerate(zip(got, want)) if a != b), None)
     if j is not None:
-        r = acm.Load(tiny_models[name], 0, engine=eng)
-        lg = r.Forward(p)
-        for t in got[:j]:
-            lg = r.Forward([t])
-        assert got[j] == oracle.sample(lg, 0.7, 40, 0.0, oracle.uniform(77, j))
-        o.reset()
-        lo = o.forward(p)
-        for t in got[:j]:
-            lo = o.forward([t])
-        assert rel_l2(lg, lo) < 1e-3
-        r.close()
-    m.close()
+        ok = reachable(oracle, r["logits"][j], 0.7, 40, 0.0, oracle.uniform(77, j))
+        assert len(ok) > 1 and got[j] in ok, (j, got[j], want[j], ok)
 
 
 def test_generate_stops_on_eos(acm, eng, oracle, synth, tiny_models):
