@@ -74,6 +74,7 @@ SIGNATURES = {
     "acm_matmul": (C.c_int, [P, C.c_uint32, P, C.c_int64, C.c_int64, P, C.c_int32, P]),
     "acm_matmul_dev": (C.c_int, [P, C.c_uint32, P, C.c_int64, C.c_int64, P, C.c_int32, P]),
     "acm_sample_logits": (C.c_int, [P, P, C.c_int32, C.POINTER(CSampler), C.c_uint64, C.POINTER(C.c_int32)]),
+    "acm_sample_dev_noalloc": (C.c_int, [P, P, C.c_int64, C.c_int32, C.c_int32, P, P, P]),
     "acm_engine_stream": (P, [P]),
     "acm_engine_sync": (C.c_int, [P]),
     "acm_model_last_timing": (C.c_int, [P, C.POINTER(C.c_double), C.POINTER(C.c_double)]),

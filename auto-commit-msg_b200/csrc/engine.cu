@@ -1419,3 +1419,25 @@ ACM_API int acm_sample_logits(acm_engine *e, const float *host_logits, int32_t n
 }
 
 }  // extern "C"
+
+namespace acm {
+int sample_noalloc(int dev, cudaStream_t st, const float *d_logits, int64_t ld, int nrows, int vocab,
+                   const acm_sampler *samplers, const uint64_t *steps, int32_t *d_out, std::string *err);
+}
+
+extern "C" {
+
+// The sampler on device logits with its scratch in a fixed buffer of the
+// library image (k_noalloc.cu): nothing is allocated, nothing is copied back,
+// nothing waits; the ids land in d_out when the engine stream reaches them.
+ACM_API int acm_sample_dev_noalloc(acm_engine *e, const float *d_logits, int64_t ld, int32_t nrows, int32_t vocab,
+                                   const acm_sampler *samplers, const uint64_t *steps, int32_t *d_out) {
+    if (!e) return ACM_ERR_INVALID;
+    CK_E(cudaSetDevice(e->device));
+    std::string msg;
+    const int rc = acm::sample_noalloc(e->device, e->stream, d_logits, ld, nrows, vocab, samplers, steps, d_out, &msg);
+    if (rc == 0) return ACM_OK;
+    return set_eerr(e, rc == 1 ? ACM_ERR_INVALID : ACM_ERR_CUDA, msg);
+}
+
+}  // extern "C"

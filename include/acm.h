@@ -179,6 +179,22 @@ ACM_API int acm_matmul_dev(acm_engine *e, uint32_t ggml_type, const void *d_w, i
 ACM_API int acm_sample_logits(acm_engine *e, const float *host_logits, int32_t n, const acm_sampler *s,
                               uint64_t step, int32_t *tok_out);
 
+/* No counterpart in the reference (its sampler works on a Go slice).  The
+ * sampler of acm_sample_logits on nrows device-resident logits rows (row r at
+ * d_logits + r * ld, vocab floats), row r drawn with samplers[r] at step
+ * steps[r] (samplers NULL: greedy; steps NULL: 0), ids written to the device
+ * array d_out.  It allocates nothing: for callers that must not touch the
+ * device allocator mid-decode (cudaMalloc / cudaFree synchronise the device,
+ * and fail once the KV cache has taken the free HBM), the scratch is a fixed
+ * 4 MiB buffer of the library image, one per device.  Limits: nrows <= 64,
+ * vocab <= 262144; beyond them the call returns ACM_ERR_INVALID and says so.
+ * Enqueued on the engine stream without waiting.  The buffer is shared by all
+ * engines on a device, so calls must not overlap (one stream, or ordered by
+ * the caller).  The first call on a device looks up the buffer's address
+ * (cudaGetSymbolAddress); make it before beginning any stream capture. */
+ACM_API int acm_sample_dev_noalloc(acm_engine *e, const float *d_logits, int64_t ld, int32_t nrows, int32_t vocab,
+                                   const acm_sampler *samplers, const uint64_t *steps, int32_t *d_out);
+
 /* Engine stream (cudaStream_t) and synchronisation, for callers that time
  * device work with their own events. */
 ACM_API void *acm_engine_stream(acm_engine *e);
