@@ -2,6 +2,8 @@
 // persistent decode kernel: paged cache addressing and the per-head
 // RMSNorm + RoPE of model.go:362-382.
 #pragma once
+#include <float.h>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "quant.cuh"
@@ -36,6 +38,278 @@ __device__ __forceinline__ void head_norm_rope(float *v, const float *nw, const 
         v[ib] = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
     }
     __syncwarp();
+}
+
+// The same per-head RMSNorm + RoPE on a head already held in registers (lane
+// owns elements lane + 32e) with its norm weights (nw, when has_nw) and its
+// rope table entries (cs[j] for pair lane + 32j) preloaded; the result is
+// written to v (shared memory).  Same arithmetic as head_norm_rope.
+template <int HD, int NR>
+__device__ __forceinline__ void norm_rope_regs(float *v, const float (&x)[HD / 32], bool has_nw,
+                                               const float (&nw)[HD / 32], const float2 (&cs)[NR], int half,
+                                               int interleaved, float eps, int lane) {
+    constexpr int PER = HD / 32;
+    if (has_nw) {
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < PER; e++) ss = fmaf(x[e], x[e], ss);
+        ss = warp_sum(ss);
+        const float sc = rms_scale(ss, HD, eps);
+#pragma unroll
+        for (int e = 0; e < PER; e++) v[lane + 32 * e] = __fmul_rn(__fmul_rn(x[e], sc), nw[e]);
+    } else {
+#pragma unroll
+        for (int e = 0; e < PER; e++) v[lane + 32 * e] = x[e];
+    }
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < NR; j++) {
+        const int i = lane + 32 * j;
+        if (i < half) {
+            const int ia = interleaved ? 2 * i : i, ib = interleaved ? 2 * i + 1 : i + half;
+            const float a = v[ia], b = v[ib];
+            v[ia] = __fsub_rn(__fmul_rn(a, cs[j].x), __fmul_rn(b, cs[j].y));
+            v[ib] = __fadd_rn(__fmul_rn(a, cs[j].y), __fmul_rn(b, cs[j].x));
+        }
+    }
+    __syncwarp();
+}
+
+// Stride (floats) of one partial row of the decode attention: HD values of
+// sum e*v, then max and sum e, padded to 16 bytes for bulk copies.
+__host__ __device__ constexpr int dec_part_stride(int HD) { return HD + 4; }
+
+// Shared-memory floats one decode attention item needs (a multiple of 4).
+__host__ __device__ constexpr int dec_item_floats(int HD, int CH, int G) {
+    return (G * (HD + 4) + CH * (HD + 4) + CH * HD + G * CH + 2 * G + (HD < 128 ? HD : 0) + 4 + 3) & ~3;
+}
+
+// Cache offsets of a decode attention item, without the layer term: `base`
+// of the slice's first position (the slice lies in one page, CH dividing the
+// page size) and `newo` of the new position `pos`; both include kv head g.
+__device__ __forceinline__ void dec_item_offsets(const KVDesc &kv, int seq, int pos, int g, int lo, int hd,
+                                                 int64_t &base, int64_t &newo) {
+    const int32_t *pt = kv.page_table + (int64_t)seq * kv.max_pages;
+    base = ((int64_t)pt[lo / kv.page_size] * kv.page_size + (lo % kv.page_size)) * kv.kvd + g * hd;
+    newo = ((int64_t)pt[pos / kv.page_size] * kv.page_size + (pos % kv.page_size)) * kv.kvd + g * hd;
+}
+
+// One decode attention item: token t (new position pos), kv head g,
+// positions [c*CH, c*CH + CH) -- model.go:362-408 for that slice,
+// flash-decoding style -- run by 128 threads (gtid 0..127) that synchronise
+// on named barrier `bid`.  The item whose slice holds `pos` also normalises,
+// ropes and appends the new key/value (model.go:362-382).  With more than one
+// slice, each writes an unnormalised partial (sum e*v, max, sum e) and the
+// last slice of (t, g) to finish merges them.  sm: dec_item_floats(HD, CH,
+// G) floats, 16-byte aligned.  base / newo: dec_item_offsets.
+//
+// Latency is what matters at this size (a few KB per item): the cached rows
+// are requested first, every other global load is issued before any is
+// consumed, and the merge pulls whole partial rows into shared memory with
+// asynchronous copies (one round trip per head for up to
+// (CH*(HD+4) + CH*HD) / (HD+4) slices).  Register use stays small so the
+// item also runs inside the persistent decode kernel's 96-register budget.
+template <int HD, int CH>
+__device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const float *k_nw, const AttnDesc &a,
+                                 const KVDesc &kv, int layer, int t, int pos, int g, int c, int64_t base,
+                                 int64_t newo, float *sm, int gtid, int bid) {
+    constexpr int PER = HD / 32, QS = HD + 4, KS = HD + 4, NR = (HD / 2 + 31) / 32;
+    constexpr int GROUPS = 128 / HD, PS = dec_part_stride(HD);
+    static_assert(CH == 16 || CH == 32, "chunk must be 16 or 32 positions");
+    const int warp = gtid >> 5, lane = gtid & 31;
+    const int G = a.n_head / a.n_head_kv, nh = a.n_head, qd = nh * HD, kvd = a.n_head_kv * HD;
+    const int L = pos + 1, lo = c * CH, hi = min(L, lo + CH), n = hi - lo;
+    const int nchunk = (L + CH - 1) / CH;
+    float *qs = sm;                 // [G][QS]
+    float *ks = qs + G * QS;        // [CH][KS]   } merge: partial rows
+    float *vs = ks + CH * KS;       // [CH][HD]   }
+    float *sc = vs + CH * HD;       // [G][CH]
+    float *stat = sc + G * CH;      // [G][2]
+    float *gred = stat + 2 * G;     // [HD] second position group (HD < 128)
+    int *flag = reinterpret_cast<int *>(gred + (HD < 128 ? HD : 0));
+    const bool has_new = pos >= lo && pos < hi;
+    const int ncopy = has_new ? n - 1 : n;
+    const bool kwarp = has_new && warp == (G & 3);
+    const int half = r.rope_dim / 2;
+    const int64_t lofs = (int64_t)layer * kv.layer_stride;
+
+    // ---- cached rows of the slice: asynchronous copies, all in flight ----
+    {
+        constexpr int CPR = HD / 4;  // 16-byte pieces per row
+        const float *kb = kv.k + lofs + base, *vb = kv.v + lofs + base;
+        for (int i = gtid; i < ncopy * CPR * 2; i += 128) {
+            const int which = i / (ncopy * CPR), rem = i - which * ncopy * CPR;
+            const int p = rem / CPR, piece = rem - p * CPR;
+            if (which) cp_async16(vs + p * HD + piece * 4, vb + (int64_t)p * kv.kvd + piece * 4);
+            else cp_async16(ks + p * KS + piece * 4, kb + (int64_t)p * kv.kvd + piece * 4);
+        }
+    }
+    // ---- query heads (and the new key): loads, then norm + rope ----
+    {
+        float nq[PER];
+        float2 cs[NR];
+#pragma unroll
+        for (int e = 0; e < PER; e++) nq[e] = q_nw ? q_nw[lane + 32 * e] : 0.f;
+#pragma unroll
+        for (int j = 0; j < NR; j++) {
+            const int i = lane + 32 * j;
+            cs[j] = i < half ? r.tab[(int64_t)pos * half + i] : make_float2(0.f, 0.f);
+        }
+        for (int h = warp; h < G; h += 4) {
+            const float *src = a.q + (int64_t)t * qd + (int64_t)(g * G + h) * HD;
+            float qv[PER];
+#pragma unroll
+            for (int e = 0; e < PER; e++) qv[e] = __ldcg(src + lane + 32 * e);
+            norm_rope_regs<HD, NR>(qs + h * QS, qv, q_nw != nullptr, nq, cs, half, r.interleaved, r.eps, lane);
+        }
+        if (kwarp) {
+            const float *ksrc = r.k + (int64_t)t * kvd + g * HD, *vsrc = r.v + (int64_t)t * kvd + g * HD;
+            float kx[PER], nk[PER];
+            float *kn = ks + (n - 1) * KS, *vn = vs + (n - 1) * HD;
+#pragma unroll
+            for (int e = 0; e < PER; e++) {
+                kx[e] = __ldcg(ksrc + lane + 32 * e);
+                vn[lane + 32 * e] = __ldcg(vsrc + lane + 32 * e);
+                nk[e] = k_nw ? k_nw[lane + 32 * e] : 0.f;
+            }
+            norm_rope_regs<HD, NR>(kn, kx, k_nw != nullptr, nk, cs, half, r.interleaved, r.eps, lane);
+            float *kd = kv.k + lofs + newo, *vd = kv.v + lofs + newo;
+#pragma unroll
+            for (int e = 0; e < PER; e++) {
+                kd[lane + 32 * e] = kn[lane + 32 * e];
+                vd[lane + 32 * e] = vn[lane + 32 * e];
+            }
+        }
+    }
+    cp_async_wait_all();
+    named_sync(bid, 128);
+
+    // ---- scores (one lane per (head, position)) and the slice softmax ----
+    for (int b0 = warp * 32; b0 < G * CH; b0 += 128) {
+        const int i = b0 + lane, h = i / CH, p = i - h * CH;
+        const bool ok = i < G * CH && p < n;
+        float s = -FLT_MAX;
+        if (ok) {
+            const float4 *qh = reinterpret_cast<const float4 *>(qs + h * QS);
+            const float4 *kp = reinterpret_cast<const float4 *>(ks + p * KS);
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+            for (int d4 = 0; d4 < HD / 4; d4++) {
+                const float4 x = qh[d4], y = kp[d4];
+                acc.x = fmaf(x.x, y.x, acc.x);
+                acc.y = fmaf(x.y, y.y, acc.y);
+                acc.z = fmaf(x.z, y.z, acc.z);
+                acc.w = fmaf(x.w, y.w, acc.w);
+            }
+            s = __fmul_rn((acc.x + acc.y) + (acc.z + acc.w), a.scale);
+        }
+        float mx = s;
+#pragma unroll
+        for (int o = CH / 2; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float e = ok ? fast_exp(__fsub_rn(s, mx)) : 0.f;
+        float sum = e;
+#pragma unroll
+        for (int o = CH / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (i < G * CH) {
+            sc[h * CH + p] = nchunk == 1 ? __fdiv_rn(e, sum) : e;
+            if (p == 0) {
+                stat[2 * h] = mx;
+                stat[2 * h + 1] = sum;
+            }
+        }
+    }
+    named_sync(bid, 128);
+
+    // ---- P.V, head by head; single chunk: the output, else the partial ----
+    const int d = gtid % HD, gp = gtid / HD;
+    for (int h = 0; h < G; h++) {
+        const float *sh = sc + h * CH;
+        float acc = 0.f;
+#pragma unroll 4
+        for (int p = gp; p < n; p += GROUPS) acc = fmaf(sh[p], vs[p * HD + d], acc);
+        if (GROUPS > 1) {
+            if (gp > 0) gred[d] = acc;
+            named_sync(bid, 128);
+            if (gp == 0) acc += gred[d];
+            named_sync(bid, 128);
+        }
+        if (gp == 0) {
+            if (nchunk == 1) {
+                a.out[(int64_t)t * qd + (int64_t)(g * G + h) * HD + d] = acc;
+            } else {
+                float *pp = a.part + (((int64_t)t * nh + g * G + h) * a.nsplit + c) * PS;
+                pp[d] = acc;
+                if (d == 0) {
+                    pp[HD] = stat[2 * h];
+                    pp[HD + 1] = stat[2 * h + 1];
+                }
+            }
+        }
+    }
+    if (nchunk == 1) {
+        named_sync(bid, 128);
+        return;
+    }
+
+    // ---- arrival count; the last slice of (t, g) merges ----
+    __threadfence();
+    named_sync(bid, 128);
+    if (gtid == 0) {
+        int *cnt = a.counter + (int64_t)t * a.n_head_kv + g;
+        const int old = atomicAdd(cnt, 1);
+        const int last = old == nchunk - 1;
+        if (last) *cnt = 0;  // ready for the next step
+        *flag = last;
+    }
+    named_sync(bid, 128);
+    if (*flag) {
+        __threadfence();
+        // merge buffer: the ks..vs region, `cap` partial rows at a time
+        float *buf = ks;
+        constexpr int CAP = (CH * KS + CH * HD) / PS;
+        for (int h = 0; h < G; h++) {
+            const float *ph = a.part + ((int64_t)t * nh + g * G + h) * a.nsplit * PS;
+            float M = -FLT_MAX, num = 0.f, den = 0.f;
+            for (int c0 = 0; c0 < nchunk; c0 += CAP) {
+                const int nt = min(CAP, nchunk - c0);
+                for (int i = gtid; i < nt * (PS / 4); i += 128) {
+                    const int cc = i / (PS / 4), piece = i - cc * (PS / 4);
+                    cp_async16(buf + cc * PS + piece * 4, ph + (int64_t)(c0 + cc) * PS + piece * 4);
+                }
+                cp_async_wait_all();
+                named_sync(bid, 128);
+                float mt = -FLT_MAX;
+                for (int cc = 0; cc < nt; cc++) mt = fmaxf(mt, buf[cc * PS + HD]);
+                const float Mn = fmaxf(M, mt);
+                if (c0 > 0) {  // contexts longer than one buffer: rescale what came before
+                    const float r0 = fast_exp(M - Mn);
+                    num *= r0;
+                    den *= r0;
+                }
+                M = Mn;
+                for (int cc = gp; cc < nt; cc += GROUPS) {
+                    const float w = fast_exp(buf[cc * PS + HD] - M);
+                    num = fmaf(w, buf[cc * PS + d], num);
+                    den = fmaf(w, buf[cc * PS + HD + 1], den);
+                }
+                named_sync(bid, 128);
+            }
+            if (GROUPS > 1) {
+                if (gp > 0) {
+                    gred[d] = num;
+                    if (d == 0) stat[0] = den;
+                }
+                named_sync(bid, 128);
+                if (gp == 0) {
+                    num += gred[d];
+                    den += stat[0];
+                }
+                named_sync(bid, 128);
+            }
+            if (gp == 0) a.out[(int64_t)t * qd + (int64_t)(g * G + h) * HD + d] = num / den;
+        }
+    }
+    named_sync(bid, 128);
 }
 
 }  // namespace acm

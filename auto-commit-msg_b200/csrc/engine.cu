@@ -402,6 +402,10 @@ bool mega_ready(acm_model *m) {
     int coop = 0;
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->e->device);
     if (!coop) return false;
+    if (decode_launch(m->dplan, nullptr, c.head_dim, m->e->stream) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
     if (dalloc(m, &m->d_dtable, m->dplan.table.size()) != cudaSuccess) return false;
     if (cudaMemcpy(m->d_dtable, m->dplan.table.data(), sizeof(DecPhase) * m->dplan.table.size(),
                    cudaMemcpyHostToDevice) != cudaSuccess)
@@ -427,6 +431,7 @@ int mega_step(acm_model *m, bool greedy) {
     A.sb = m->dplan.sb;
     A.ring_off = m->dplan.ring_off;
     A.area_off = m->dplan.area_off;
+    A.meta_off = m->dplan.meta_off;
     A.attn_group_floats = m->dplan.attn_group_floats;
     A.r = RopeDesc{m->q, m->k, m->v, nullptr, nullptr, m->rope_tab, c.n_head, c.n_head_kv, hd, c.rope_dim,
                    c.rope_interleaved, c.rms_eps};
@@ -444,7 +449,7 @@ int mega_step(acm_model *m, bool greedy) {
     A.hist_ld = HIST_MAX;
     A.hist_col = m->d_hist_col;
     A.trace = m->trace ? m->d_trace : nullptr;
-    CK_M(decode_launch(m->dplan, A, hd, st));
+    CK_M(decode_launch(m->dplan, &A, hd, st));
     if (!greedy) {
         CK_M(cudaMemsetAsync(m->d_amax, 0, sizeof(unsigned long long), st));
         int rc = sample_pass(m, 1, false);
@@ -808,7 +813,8 @@ ACM_API int acm_model_finalize(acm_model *m) {
     CK_M(dalloc(m, &m->hb2, T * F));
     m->dec_nsplit = (c.max_ctx + 31) / 32;  // 32-position chunks of the decode attention
     const size_t part_rows = std::max<size_t>((size_t)PART_TOKSPLIT, (size_t)m->tdec * m->dec_nsplit);
-    CK_M(dalloc(m, &m->part, part_rows * c.n_head * (hd + 2)));
+    // rows of hd + 4 floats: the decode attention's partial stride (dec_part_stride)
+    CK_M(dalloc(m, &m->part, part_rows * c.n_head * (hd + 4)));
     CK_M(dalloc(m, &m->d_attn_cnt, (size_t)m->tdec * c.n_head_kv));
     CK_M(cudaMemset(m->d_attn_cnt, 0, sizeof(int) * (size_t)m->tdec * c.n_head_kv));
     CK_M(dalloc(m, &m->logits, (size_t)m->max_seqs * c.vocab));

@@ -29,58 +29,88 @@ __host__ __device__ inline size_t x_bytes(int64_t k, int mt, int lpr) {
     return (b + 127) & ~size_t(127);
 }
 
+// Offset of activation element k in the x area (unit path: permuted into
+// unit order with a bank swizzle; wide path: natural order, 4 floats of
+// padding per 256).
+template <int T>
+__device__ __forceinline__ int x_off(int k, int K, bool wide) {
+    if (wide) return (k >> 8) * 260 + (k & 255);
+    int u, j;
+    pos_unit<T>(k, K, u, j);
+    return u * 32 + (((j >> 2) ^ (u & 7)) << 2) + (j & 3);
+}
+
+// Stage the activations (RMSNorm-ed when norm_w is set, model.go:213-222)
+// into the x area.  The activations were written by other CTAs an instant
+// ago, so each thread issues all of its loads (XB per token at a time, with
+// the norm weights) before using any: one round trip instead of K / NC.
 template <int T, int MT>
 __device__ __forceinline__ void prep_x(const GemvArgs &a, float *xs, float *xsum, float *red) {
     constexpr int NCW = Cfg<MT>::NCW, NC = NCW * 32;
+    constexpr int XB = MT <= 2 ? 8 : 4;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = a.k;
-    float sc[MT];
+    const bool wide = a.lpr != 0;
+    const bool norm = a.norm_w != nullptr;
+    const size_t xstr = wide ? (size_t)(K / 256) * 260 : (size_t)K;
+    // norm weights first: in flight together with the activations
+    float nw[XB];
+    const bool one = K <= XB * NC;
+    if (norm && one)
 #pragma unroll
-    for (int m = 0; m < MT; m++) sc[m] = 1.0f;
-    if (a.norm_w) {
-        float ss[MT];
+        for (int j = 0; j < XB; j++) nw[j] = j * NC + tid < K ? a.norm_w[j * NC + tid] : 0.f;
+    float ss[MT];
 #pragma unroll
-        for (int m = 0; m < MT; m++) ss[m] = 0.f;
-        for (int k = tid; k < K; k += NC)
+    for (int m = 0; m < MT; m++) ss[m] = 0.f;
+    // pass 1: raw values into the x area (and sum of squares)
+    for (int k0 = 0; k0 < K; k0 += XB * NC) {
+        float v[XB][MT];
 #pragma unroll
-            for (int m = 0; m < MT; m++)
-                if (m < a.m) {
-                    const float v = __ldcg(a.x + (int64_t)m * a.ldx + k);
-                    ss[m] = fmaf(v, v, ss[m]);
+        for (int j = 0; j < XB; j++) {
+            const int k = k0 + j * NC + tid;
+#pragma unroll
+            for (int m = 0; m < MT; m++) v[j][m] = (k < K && m < a.m) ? __ldcg(a.x + (int64_t)m * a.ldx + k) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < XB; j++) {
+            const int k = k0 + j * NC + tid;
+            if (k < K) {
+                const int off = x_off<T>(k, K, wide);
+#pragma unroll
+                for (int m = 0; m < MT; m++) {
+                    ss[m] = fmaf(v[j][m], v[j][m], ss[m]);
+                    xs[m * xstr + off] = v[j][m];
                 }
+            }
+        }
+    }
+    if (norm) {
+        // pass 2 (same thread, same elements): scale by the row's RMS and the weight
 #pragma unroll
         for (int m = 0; m < MT; m++) {
             const float w = warp_sum(ss[m]);
             if (lane == 0) red[warp * MT + m] = w;
         }
         named_sync(1, NC);
+        float sc[MT];
 #pragma unroll
         for (int m = 0; m < MT; m++) {
             float t = 0.f;
             for (int w = 0; w < NCW; w++) t += red[w * MT + m];
             sc[m] = rms_scale(t, K, a.eps);
         }
-    }
-    const bool wide = a.lpr != 0;
-    for (int k = tid; k < K; k += NC) {
-        int off;
-        if (wide) {
-            off = (k >> 8) * 260 + (k & 255);
-        } else {
-            int u, j;
-            pos_unit<T>(k, K, u, j);
-            off = u * 32 + (((j >> 2) ^ (u & 7)) << 2) + (j & 3);
-        }
-        const float nw = a.norm_w ? a.norm_w[k] : 1.0f;
-        const size_t xstr = wide ? (size_t)(K / 256) * 260 : (size_t)K;
+        for (int k0 = 0; k0 < K; k0 += XB * NC) {
 #pragma unroll
-        for (int m = 0; m < MT; m++) {
-            float v = 0.f;
-            if (m < a.m) {
-                v = __ldcg(a.x + (int64_t)m * a.ldx + k);
-                if (a.norm_w) v = __fmul_rn(__fmul_rn(v, sc[m]), nw);
+            for (int j = 0; j < XB; j++) {
+                const int k = k0 + j * NC + tid;
+                if (k < K) {
+                    const float wk = one ? nw[j] : a.norm_w[k];
+                    const int off = x_off<T>(k, K, wide);
+#pragma unroll
+                    for (int m = 0; m < MT; m++)
+                        if (m < a.m) xs[m * xstr + off] = __fmul_rn(__fmul_rn(xs[m * xstr + off], sc[m]), wk);
+                }
             }
-            xs[m * xstr + off] = v;
         }
     }
     named_sync(1, NC);
@@ -120,10 +150,23 @@ __device__ __forceinline__ void prep_x(const GemvArgs &a, float *xs, float *xsum
     }
 }
 
-// Epilogue of one finished row n (values for tokens 0..m_used-1).
+// Residual values of row n for the EPI_ADD epilogue, loaded before the row's
+// dot products so the read overlaps them.
+template <int MT>
+__device__ __forceinline__ void prefetch_res(const GemvSeg &s, int n, int m_used, bool active, float (&res)[MT]) {
+#pragma unroll
+    for (int m = 0; m < MT; m++)
+        res[m] = (active && s.epi == EPI_ADD && m < m_used)
+                     ? __ldcg(s.y + (int64_t)(s.yrow ? s.yrow[m] : m) * s.ldy + n)
+                     : 0.f;
+}
+
+// Epilogue of one finished row n (values for tokens 0..m_used-1); res holds
+// the residual values (prefetch_res) for EPI_ADD.
 template <int MT>
 __device__ __forceinline__ void row_out(const GemvSeg &s, int n, int m_used, const float (&acc)[MT],
-                                        const float (&acc2)[MT], unsigned long long (&best)[MT]) {
+                                        const float (&acc2)[MT], const float (&res)[MT],
+                                        unsigned long long (&best)[MT]) {
 #pragma unroll
     for (int m = 0; m < MT; m++) {
         if (m < m_used) {
@@ -131,7 +174,7 @@ __device__ __forceinline__ void row_out(const GemvSeg &s, int n, int m_used, con
             if (s.bias) v += s.bias[n];
             float *yp = s.y + (int64_t)(s.yrow ? s.yrow[m] : m) * s.ldy + n;
             if (s.epi == EPI_ADD) {
-                *yp = __ldcg(yp) + v;
+                *yp = res[m] + v;
             } else if (s.epi == EPI_SWIGLU) {
                 const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, fast_exp(-v)));
                 *yp = __fmul_rn(__fmul_rn(v, sg), acc2[m]);
@@ -184,6 +227,8 @@ __device__ __forceinline__ void consume_unit(const GemvArgs &a, const GemvSeg &s
         const uint8_t *buf = stg + (size_t)slot * a.stage_bytes;
         for (int rr = warp; rr < rbn - ra; rr += NCW) {
             const int n = ra + rr;
+            float res[MT];
+            prefetch_res<MT>(s, n, a.m, lane == 0, res);
             const uint8_t *rp = buf + ((int64_t)n * s.rb - a0);
             float acc[MT], acc2[MT];
 #pragma unroll
@@ -201,7 +246,7 @@ __device__ __forceinline__ void consume_unit(const GemvArgs &a, const GemvSeg &s
                 acc[m] = warp_sum(acc[m]);
                 if (pair) acc2[m] = warp_sum(acc2[m]);
             }
-            if (lane == 0) row_out<MT>(s, n, a.m, acc, acc2, best);
+            if (lane == 0) row_out<MT>(s, n, a.m, acc, acc2, res, best);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
@@ -239,6 +284,8 @@ __device__ __forceinline__ void consume_wide(const GemvArgs &a, const GemvSeg &s
                 const int rr = gb + lane / lpr;
                 const bool valid = rr < rbn - ra;
                 const int n = ra + rr;
+                float res[MT];
+                prefetch_res<MT>(s, n, a.m, valid && sub == 0, res);
                 float acc[MT], acc2[MT];
 #pragma unroll
                 for (int m = 0; m < MT; m++) acc[m] = acc2[m] = 0.f;
@@ -258,7 +305,7 @@ __device__ __forceinline__ void consume_wide(const GemvArgs &a, const GemvSeg &s
                         acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
                         if (pair) acc2[m] += __shfl_xor_sync(0xffffffffu, acc2[m], o);
                     }
-                if (valid && sub == 0) row_out<MT>(s, n, a.m, acc, acc2, best);
+                if (valid && sub == 0) row_out<MT>(s, n, a.m, acc, acc2, res, best);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);

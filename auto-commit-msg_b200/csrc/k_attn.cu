@@ -171,160 +171,15 @@ constexpr int ATT_CHUNK = 32;
 template <int HD>
 __global__ void __launch_bounds__(128) k_attn_decode(const RopeDesc r, const AttnDesc a, const KVDesc kv, int layer,
                                                      TokMeta tm) {
-    extern __shared__ float sm[];
-    constexpr int PER = HD / 32;
+    extern __shared__ __align__(16) float sm[];
     const int t = blockIdx.x, g = blockIdx.y, c = blockIdx.z;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int G = a.n_head / a.n_head_kv, nh = a.n_head, qd = nh * HD, kvd = a.n_head_kv * HD;
-    if (tid == 0) pdl_trigger();
+    if (threadIdx.x == 0) pdl_trigger();
     pdl_wait();
-    const int seq = tm.seq[t], pos = tm.pos[t], L = pos + 1;
-    const int lo = c * ATT_CHUNK;
-    if (lo >= L) return;
-    const int hi = min(L, lo + ATT_CHUNK), n = hi - lo;
-    const int nchunk = (L + ATT_CHUNK - 1) / ATT_CHUNK;
-    float *qs = sm;                       // [G][HD]
-    float *ks = qs + G * HD;              // [ATT_CHUNK][HD]
-    float *vs = ks + ATT_CHUNK * HD;      // [ATT_CHUNK][HD]
-    float *sc = vs + ATT_CHUNK * HD;      // [G][ATT_CHUNK]
-    float *stat = sc + G * ATT_CHUNK;     // [G][2]
-    float *red = stat + 2 * G;            // [G][HD] second position group (HD = 64)
-    int *flag = reinterpret_cast<int *>(red + G * HD);
-    const bool has_new = pos >= lo && pos < hi;
-    // stage the cached rows (all copies in flight together)
-    const int ncopy = has_new ? n - 1 : n;
-    constexpr int CPR = HD / 4;  // 16-byte pieces per row
-    // the chunk lies in one page (ATT_CHUNK divides the page size): one lookup
-    const int64_t base = (int64_t)layer * kv.layer_stride +
-                         ((int64_t)kv.page_table[(int64_t)seq * kv.max_pages + lo / kv.page_size] * kv.page_size +
-                          (lo % kv.page_size)) * kv.kvd + g * HD;
-    for (int i = tid; i < ncopy * CPR * 2; i += 128) {
-        const int which = i / (ncopy * CPR), rem = i - which * ncopy * CPR;
-        const int p = rem / CPR, piece = rem - p * CPR;
-        const float *row = (which ? kv.v : kv.k) + base + (int64_t)p * kv.kvd;
-        cp_async16((which ? vs : ks) + p * HD + piece * 4, row + piece * 4);
-    }
-    // query heads of this group: norm + rope (each chunk CTA redoes this)
-    for (int h = warp; h < G; h += 4) {
-        const float *src = a.q + (int64_t)t * qd + (int64_t)(g * G + h) * HD;
-        for (int d = lane; d < HD; d += 32) qs[h * HD + d] = src[d];
-        __syncwarp();
-        head_norm_rope<HD>(qs + h * HD, r.q_nw, r, pos, lane);
-    }
-    if (has_new && warp == (G & 3)) {
-        // the new position: k = rope(norm(k)), v as produced; into the cache
-        float *kn = ks + (n - 1) * HD, *vn = vs + (n - 1) * HD;
-        const float *ksrc = r.k + (int64_t)t * kvd + g * HD, *vsrc = r.v + (int64_t)t * kvd + g * HD;
-        for (int d = lane; d < HD; d += 32) {
-            kn[d] = ksrc[d];
-            vn[d] = vsrc[d];
-        }
-        __syncwarp();
-        head_norm_rope<HD>(kn, r.k_nw, r, pos, lane);
-        float *kd = const_cast<float *>(kv_row(kv.k, kv, layer, seq, pos)) + g * HD;
-        float *vd = const_cast<float *>(kv_row(kv.v, kv, layer, seq, pos)) + g * HD;
-        for (int d = lane; d < HD; d += 32) {
-            kd[d] = kn[d];
-            vd[d] = vn[d];
-        }
-    }
-    cp_async_wait_all();
-    __syncthreads();
-    // scores
-    for (int p = warp; p < n; p += 4) {
-        float kk[PER];
-#pragma unroll
-        for (int e = 0; e < PER; e++) kk[e] = ks[p * HD + lane + 32 * e];
-        for (int h = 0; h < G; h++) {
-            float s = 0.f;
-#pragma unroll
-            for (int e = 0; e < PER; e++) s = fmaf(qs[h * HD + lane + 32 * e], kk[e], s);
-            s = warp_sum(s);
-            if (lane == 0) sc[h * ATT_CHUNK + p] = __fmul_rn(s, a.scale);
-        }
-    }
-    __syncthreads();
-    for (int h = warp; h < G; h += 4) {
-        float *s = sc + h * ATT_CHUNK;
-        float mx = -FLT_MAX;
-        for (int i = lane; i < n; i += 32) mx = fmaxf(mx, s[i]);
-        mx = warp_max(mx);
-        float sum = 0.f;
-        for (int i = lane; i < n; i += 32) {
-            const float e = fast_exp(__fsub_rn(s[i], mx));
-            s[i] = e;
-            sum += e;
-        }
-        sum = warp_sum(sum);
-        __syncwarp();
-        if (nchunk == 1)
-            for (int i = lane; i < n; i += 32) s[i] = __fdiv_rn(s[i], sum);
-        if (lane == 0) {
-            stat[2 * h] = mx;
-            stat[2 * h + 1] = sum;
-        }
-    }
-    __syncthreads();
-    constexpr int GROUPS = 128 / HD;
-    const int d = tid % HD, grp = tid / HD;
-    float acc[8];
-#pragma unroll
-    for (int h = 0; h < 8; h++) acc[h] = 0.f;
-    for (int p = grp; p < n; p += GROUPS) {
-        const float v = vs[p * HD + d];
-#pragma unroll
-        for (int h = 0; h < 8; h++)
-            if (h < G) acc[h] = fmaf(sc[h * ATT_CHUNK + p], v, acc[h]);
-    }
-    if (GROUPS > 1) {
-        if (grp > 0)
-            for (int h = 0; h < G; h++) red[h * HD + d] = acc[h];
-        __syncthreads();
-        if (grp == 0)
-            for (int h = 0; h < G; h++) acc[h] += red[h * HD + d];
-    }
-    if (nchunk == 1) {
-        if (grp == 0)
-            for (int h = 0; h < G; h++) a.out[(int64_t)t * qd + (int64_t)(g * G + h) * HD + d] = acc[h];
-        return;
-    }
-    // partial for this chunk; the last chunk CTA to arrive merges
-    if (grp == 0)
-        for (int h = 0; h < G; h++) {
-            float *pp = a.part + (((int64_t)t * nh + g * G + h) * a.nsplit + c) * (HD + 2);
-            pp[d] = acc[h];
-            if (d == 0) {
-                pp[HD] = stat[2 * h];
-                pp[HD + 1] = stat[2 * h + 1];
-            }
-        }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        int *cnt = a.counter + (int64_t)t * a.n_head_kv + g;
-        const int old = atomicAdd(cnt, 1);
-        const int last = old == nchunk - 1;
-        if (last) *cnt = 0;  // ready for the next step
-        *flag = last;
-    }
-    __syncthreads();
-    if (!*flag) return;
-    __threadfence();
-    if (grp != 0) return;
-    for (int h = 0; h < G; h++) {
-        const float *pp = a.part + ((int64_t)t * nh + g * G + h) * a.nsplit * (HD + 2);
-        float mx = -FLT_MAX;
-#pragma unroll 8
-        for (int s = 0; s < nchunk; s++) mx = fmaxf(mx, __ldcg(pp + s * (HD + 2) + HD));
-        float num = 0.f, den = 0.f;
-#pragma unroll 8
-        for (int s = 0; s < nchunk; s++) {
-            const float w = fast_exp(__ldcg(pp + s * (HD + 2) + HD) - mx);
-            num = fmaf(w, __ldcg(pp + s * (HD + 2) + d), num);
-            den = fmaf(w, __ldcg(pp + s * (HD + 2) + HD + 1), den);
-        }
-        a.out[(int64_t)t * qd + (int64_t)(g * G + h) * HD + d] = num / den;
-    }
+    const int seq = tm.seq[t], pos = tm.pos[t];
+    if (c * ATT_CHUNK > pos) return;  // beyond this token's context
+    int64_t base, newo;
+    dec_item_offsets(kv, seq, pos, g, c * ATT_CHUNK, HD, base, newo);
+    decode_attn_item<HD, ATT_CHUNK>(r, r.q_nw, r.k_nw, a, kv, layer, t, pos, g, c, base, newo, sm, threadIdx.x, 1);
 }
 
 cudaError_t attention_decode_launch(const RopeDesc &r, const AttnDesc &a, const KVDesc &kv, int layer, TokMeta tm,
@@ -336,8 +191,7 @@ cudaError_t attention_decode_launch(const RopeDesc &r, const AttnDesc &a, const 
     if (nchunk > a.nsplit) return cudaErrorInvalidValue;  // partial buffer capacity
     if (kv.page_size % ATT_CHUNK) return cudaErrorInvalidValue;
     const int HD = a.head_dim;
-    const size_t smem = ((size_t)G * HD + 2 * ATT_CHUNK * HD + (size_t)G * ATT_CHUNK + 2 * G + (size_t)G * HD + 4) *
-                        sizeof(float);
+    const size_t smem = (size_t)dec_item_floats(HD, ATT_CHUNK, G) * sizeof(float);
     dim3 grid(ntok, a.n_head_kv, nchunk);
     cudaError_t e = HD == 128 ? launch_pdl(k_attn_decode<128>, grid, dim3(128), smem, st, r, a, kv, layer, tm)
                               : launch_pdl(k_attn_decode<64>, grid, dim3(128), smem, st, r, a, kv, layer, tm);

@@ -75,171 +75,38 @@ __device__ __forceinline__ bool grid_sync(unsigned *bar, unsigned target, int *a
     return *(volatile int *)abort_flag == 0;
 }
 
-// One attention item for a 4-warp group (gtid 0..127, named barrier bid).
-template <int HD>
-__device__ void attn_item(const DecArgs &A, const DecPhase &P, int t, int g, int c, float *sm, int gtid, int bid) {
-    constexpr int PER = HD / 32;
-    const RopeDesc &r = A.r;
-    const AttnDesc &a = A.a;
-    const KVDesc &kv = A.kv;
-    const int warp = gtid >> 5, lane = gtid & 31;
-    const int G = a.n_head / a.n_head_kv, nh = a.n_head, qd = nh * HD, kvd = a.n_head_kv * HD;
-    const int seq = A.tm.seq[t], pos = A.tm.pos[t], L = pos + 1;
-    const int lo = c * DCH, hi = min(L, lo + DCH), n = hi - lo;
-    const int nchunk = (L + DCH - 1) / DCH;
-    float *qs = sm;                  // [G][HD]
-    float *ks = qs + G * HD;         // [DCH][HD]
-    float *vs = ks + DCH * HD;       // [DCH][HD]
-    float *sc = vs + DCH * HD;       // [G][DCH]
-    float *stat = sc + G * DCH;      // [G][2]
-    float *red = stat + 2 * G;       // [G][HD]
-    int *flag = reinterpret_cast<int *>(red + G * HD);
-    const bool has_new = pos >= lo && pos < hi;
-    const int ncopy = has_new ? n - 1 : n;
-    constexpr int CPR = HD / 4;
-    const int64_t base = (int64_t)P.layer * kv.layer_stride +
-                         ((int64_t)kv.page_table[(int64_t)seq * kv.max_pages + lo / kv.page_size] * kv.page_size +
-                          (lo % kv.page_size)) * kv.kvd + g * HD;
-    for (int i = gtid; i < ncopy * CPR * 2; i += 128) {
-        const int which = i / (ncopy * CPR), rem = i - which * ncopy * CPR;
-        const int p = rem / CPR, piece = rem - p * CPR;
-        cp_async16((which ? vs : ks) + p * HD + piece * 4, (which ? kv.v : kv.k) + base + (int64_t)p * kv.kvd + piece * 4);
-    }
-    RopeDesc rr = r;
-    rr.q_nw = P.q_nw;
-    rr.k_nw = P.k_nw;
-    for (int h = warp; h < G; h += 4) {
-        const float *src = a.q + (int64_t)t * qd + (int64_t)(g * G + h) * HD;
-        for (int d = lane; d < HD; d += 32) qs[h * HD + d] = __ldcg(src + d);
-        __syncwarp();
-        head_norm_rope<HD>(qs + h * HD, rr.q_nw, rr, pos, lane);
-    }
-    if (has_new && warp == (G & 3)) {
-        float *kn = ks + (n - 1) * HD, *vn = vs + (n - 1) * HD;
-        const float *ksrc = r.k + (int64_t)t * kvd + g * HD, *vsrc = r.v + (int64_t)t * kvd + g * HD;
-        for (int d = lane; d < HD; d += 32) {
-            kn[d] = __ldcg(ksrc + d);
-            vn[d] = __ldcg(vsrc + d);
-        }
-        __syncwarp();
-        head_norm_rope<HD>(kn, rr.k_nw, rr, pos, lane);
-        const int64_t off = (int64_t)P.layer * kv.layer_stride +
-                            ((int64_t)kv.page_table[(int64_t)seq * kv.max_pages + pos / kv.page_size] * kv.page_size +
-                             (pos % kv.page_size)) * kv.kvd + g * HD;
-        for (int d = lane; d < HD; d += 32) {
-            kv.k[off + d] = kn[d];
-            kv.v[off + d] = vn[d];
-        }
-    }
-    cp_async_wait_all();
-    named_sync(bid, 128);
-    for (int p = warp; p < n; p += 4) {
-        float kk[PER];
-#pragma unroll
-        for (int e = 0; e < PER; e++) kk[e] = ks[p * HD + lane + 32 * e];
-        for (int h = 0; h < G; h++) {
-            float s = 0.f;
-#pragma unroll
-            for (int e = 0; e < PER; e++) s = fmaf(qs[h * HD + lane + 32 * e], kk[e], s);
-            s = warp_sum(s);
-            if (lane == 0) sc[h * DCH + p] = __fmul_rn(s, a.scale);
-        }
-    }
-    named_sync(bid, 128);
-    for (int h = warp; h < G; h += 4) {
-        float *s = sc + h * DCH;
-        float mx = -FLT_MAX;
-        for (int i = lane; i < n; i += 32) mx = fmaxf(mx, s[i]);
-        mx = warp_max(mx);
-        float sum = 0.f;
-        for (int i = lane; i < n; i += 32) {
-            const float e = fast_exp(__fsub_rn(s[i], mx));
-            s[i] = e;
-            sum += e;
-        }
-        sum = warp_sum(sum);
-        __syncwarp();
-        if (nchunk == 1)
-            for (int i = lane; i < n; i += 32) s[i] = __fdiv_rn(s[i], sum);
-        if (lane == 0) {
-            stat[2 * h] = mx;
-            stat[2 * h + 1] = sum;
-        }
-    }
-    named_sync(bid, 128);
-    constexpr int GROUPS = 128 / HD;
-    const int d = gtid % HD, grp = gtid / HD;
-    float acc[8];
-#pragma unroll
-    for (int h = 0; h < 8; h++) acc[h] = 0.f;
-    for (int p = grp; p < n; p += GROUPS) {
-        const float v = vs[p * HD + d];
-#pragma unroll
-        for (int h = 0; h < 8; h++)
-            if (h < G) acc[h] = fmaf(sc[h * DCH + p], v, acc[h]);
-    }
-    if (GROUPS > 1) {
-        if (grp > 0)
-            for (int h = 0; h < G; h++) red[h * HD + d] = acc[h];
-        named_sync(bid, 128);
-        if (grp == 0)
-            for (int h = 0; h < G; h++) acc[h] += red[h * HD + d];
-    }
-    if (nchunk == 1) {
-        if (grp == 0)
-            for (int h = 0; h < G; h++) a.out[(int64_t)t * qd + (int64_t)(g * G + h) * HD + d] = acc[h];
-        named_sync(bid, 128);
-        return;
-    }
-    if (grp == 0)
-        for (int h = 0; h < G; h++) {
-            float *pp = a.part + (((int64_t)t * nh + g * G + h) * a.nsplit + c) * (HD + 2);
-            pp[d] = acc[h];
-            if (d == 0) {
-                pp[HD] = stat[2 * h];
-                pp[HD + 1] = stat[2 * h + 1];
-            }
-        }
-    __threadfence();
-    named_sync(bid, 128);
-    if (gtid == 0) {
-        int *cnt = a.counter + (int64_t)t * a.n_head_kv + g;
-        const int old = atomicAdd(cnt, 1);
-        const int last = old == nchunk - 1;
-        if (last) *cnt = 0;
-        *flag = last;
-    }
-    named_sync(bid, 128);
-    if (*flag) {
-        __threadfence();
-        if (grp == 0)
-            for (int h = 0; h < G; h++) {
-                const float *pp = a.part + ((int64_t)t * nh + g * G + h) * a.nsplit * (HD + 2);
-                float mx = -FLT_MAX;
-#pragma unroll 8
-                for (int s = 0; s < nchunk; s++) mx = fmaxf(mx, __ldcg(pp + s * (HD + 2) + HD));
-                float num = 0.f, den = 0.f;
-#pragma unroll 8
-                for (int s = 0; s < nchunk; s++) {
-                    const float w = fast_exp(__ldcg(pp + s * (HD + 2) + HD) - mx);
-                    num = fmaf(w, __ldcg(pp + s * (HD + 2) + d), num);
-                    den = fmaf(w, __ldcg(pp + s * (HD + 2) + HD + 1), den);
-                }
-                a.out[(int64_t)t * qd + (int64_t)(g * G + h) * HD + d] = num / den;
-            }
-    }
-    named_sync(bid, 128);
-}
+// A group's attention items are the same in every layer of a step (they
+// depend only on the tokens' positions), so the first attention phase
+// enumerates them and caches their cache offsets in shared memory.
+constexpr int DMETA = 4;  // cached items per group
+struct AttnMeta {
+    int t, g, c, pos;
+    int64_t base, newo;
+};
+struct AttnMetaGroup {
+    AttnMeta it[DMETA];
+    int n, pad_[3];
+};
 
 template <int HD>
-__device__ void attn_phase(const DecArgs &A, const DecPhase &P, float *area) {
-    const int tid = threadIdx.x, grp = tid >> 7, gtid = tid & 127;
+__device__ void attn_phase(const DecArgs &A, const DecPhase &P, float *area, AttnMetaGroup *meta) {
+    const int tid = threadIdx.x, grp = tid >> 7, gtid = tid & 127, bid = 2 + grp;
     const int nkv = A.a.n_head_kv;
     float *sm = area + grp * A.attn_group_floats;
+    AttnMetaGroup &mg = meta[grp];
+    if (P.layer > 0 && mg.n <= DMETA) {
+        for (int k = 0; k < mg.n; k++) {
+            const AttnMeta m = mg.it[k];
+            decode_attn_item<HD, DCH>(A.r, P.q_nw, P.k_nw, A.a, A.kv, P.layer, m.t, m.pos, m.g, m.c, m.base, m.newo,
+                                      sm, gtid, bid);
+        }
+        return;
+    }
     // items enumerated token by token: (t, g, c) with c < ceil(L_t / DCH)
     int total = 0;
     for (int t = 0; t < A.ntok; t++) total += nkv * ((A.tm.pos[t] + DCH) / DCH);
-    for (int item = blockIdx.x * DGROUPS + grp; item < total; item += gridDim.x * DGROUPS) {
+    int k = 0;
+    for (int item = blockIdx.x * DGROUPS + grp; item < total; item += gridDim.x * DGROUPS, k++) {
         int t = 0, rem = item;
         while (true) {
             const int cnt = nkv * ((A.tm.pos[t] + DCH) / DCH);
@@ -247,9 +114,14 @@ __device__ void attn_phase(const DecArgs &A, const DecPhase &P, float *area) {
             rem -= cnt;
             t++;
         }
-        const int nch = (A.tm.pos[t] + DCH) / DCH;
-        attn_item<HD>(A, P, t, rem / nch, rem % nch, sm, gtid, 2 + grp);
+        const int pos = A.tm.pos[t], nch = (pos + DCH) / DCH;
+        const int g = rem / nch, c = rem % nch;
+        int64_t base, newo;
+        dec_item_offsets(A.kv, A.tm.seq[t], pos, g, c * DCH, HD, base, newo);
+        if (k < DMETA && gtid == 0) mg.it[k] = AttnMeta{t, g, c, pos, base, newo};
+        decode_attn_item<HD, DCH>(A.r, P.q_nw, P.k_nw, A.a, A.kv, P.layer, t, pos, g, c, base, newo, sm, gtid, bid);
     }
+    if (P.layer == 0 && gtid == 0) mg.n = k;
 }
 
 template <int T>
@@ -293,6 +165,7 @@ __global__ void __launch_bounds__(DNT, 1) k_decode(const __grid_constant__ DecAr
     int *abort_flag = reinterpret_cast<int *>(smem + 2 * GEMV_NS_MAX * 8);
     DecPhase *ph = reinterpret_cast<DecPhase *>(smem + 256);
     float *area = reinterpret_cast<float *>(smem + A.area_off);
+    AttnMetaGroup *meta = reinterpret_cast<AttnMetaGroup *>(smem + A.meta_off);
     uint8_t *stg = smem + A.ring_off;
     // this CTA's phase table into shared memory
     const DecPhase *src = A.ph + (int64_t)blockIdx.x * A.nph;
@@ -357,7 +230,7 @@ __global__ void __launch_bounds__(DNT, 1) k_decode(const __grid_constant__ DecAr
                 cur += (uint32_t)((P.r1 - P.r0 + R - 1) / R);
             }
         } else {
-            attn_phase<HD>(A, P, area);
+            attn_phase<HD>(A, P, area, meta);
         }
     }
     if (A.amax == nullptr) {
@@ -392,8 +265,11 @@ __global__ void __launch_bounds__(DNT, 1) k_decode(const __grid_constant__ DecAr
 // ---------------------------------------------------------------------------
 static const int DSMEM_MAX = 227 * 1024;
 
+// Launch one decode step; with A == nullptr only check that a CTA of this
+// instance (DNT threads, its registers, `smem` bytes) fits on an SM, which
+// the cooperative launch of one CTA per SM needs.
 template <int HD, int... Ts>
-static cudaError_t launch_decode(const DecArgs &A, size_t smem, int grid, cudaStream_t st) {
+static cudaError_t launch_decode(const DecArgs *Ap, size_t smem, int grid, cudaStream_t st) {
     static bool attr[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -402,6 +278,13 @@ static cudaError_t launch_decode(const DecArgs &A, size_t smem, int grid, cudaSt
         if (e != cudaSuccess) return e;
         attr[dev & 63] = true;
     }
+    if (!Ap) {
+        int nb = 0;
+        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_decode<HD, Ts...>, DNT, smem);
+        if (e != cudaSuccess) return e;
+        return nb >= 1 ? cudaSuccess : cudaErrorLaunchOutOfResources;
+    }
+    const DecArgs &A = *Ap;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(DNT);
@@ -565,10 +448,11 @@ bool decode_plan(DecPlan &plan, const DecLayerDesc *layers, int n_layers, const 
             plan.table[(size_t)b * nph + p] = Q;
         }
     }
-    const int attn_floats = G * hd + 2 * DCH * hd + G * DCH + 2 * G + G * hd + 4;
+    const int attn_floats = dec_item_floats(hd, DCH, G);
     plan.attn_group_floats = (attn_floats + 31) & ~31;
     area = std::max(area, (size_t)plan.attn_group_floats * DGROUPS * 4);
-    plan.area_off = (int)(((256 + (size_t)nph * sizeof(DecPhase)) + 1023) & ~size_t(1023));
+    plan.meta_off = (int)((256 + (size_t)nph * sizeof(DecPhase) + 15) & ~size_t(15));
+    plan.area_off = (int)((plan.meta_off + DGROUPS * sizeof(AttnMetaGroup) + 1023) & ~size_t(1023));
     plan.ring_off = (int)((plan.area_off + area + 1023) & ~size_t(1023));
     plan.smem = (size_t)plan.ring_off + (size_t)plan.ns * plan.sb + 16;
     while (plan.smem > (size_t)DSMEM_MAX && plan.ns > 2) {
@@ -578,7 +462,7 @@ bool decode_plan(DecPlan &plan, const DecLayerDesc *layers, int n_layers, const 
     return plan.smem <= (size_t)DSMEM_MAX;
 }
 
-cudaError_t decode_launch(const DecPlan &plan, const DecArgs &A, int head_dim, cudaStream_t st) {
+cudaError_t decode_launch(const DecPlan &plan, const DecArgs *A, int head_dim, cudaStream_t st) {
     const bool h128 = head_dim == 128;
     switch (plan.inst) {
         case 1: return h128 ? launch_decode<128, T_Q4_K, T_Q6_K>(A, plan.smem, plan.grid, st)

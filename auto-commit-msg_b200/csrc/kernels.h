@@ -193,7 +193,7 @@ struct DecArgs {
     const DecPhase *ph;      // [grid][nph]
     int nph, ntok;
     float eps;
-    int ns, sb, ring_off, area_off, attn_group_floats;
+    int ns, sb, ring_off, area_off, meta_off, attn_group_floats;
     RopeDesc r;
     AttnDesc a;
     KVDesc kv;
@@ -225,13 +225,14 @@ struct DecLmDesc {
     unsigned long long *amax;
 };
 struct DecPlan {
-    int inst = 0, grid = 0, nph = 0, ns = 0, sb = 0, ring_off = 0, area_off = 0, attn_group_floats = 0;
+    int inst = 0, grid = 0, nph = 0, ns = 0, sb = 0, ring_off = 0, area_off = 0, meta_off = 0, attn_group_floats = 0;
     size_t smem = 0;
     std::vector<DecPhase> table;
 };
 bool decode_plan(DecPlan &plan, const DecLayerDesc *layers, int n_layers, const DecLmDesc &lm, int n_embd,
                  int n_head, int n_head_kv, int head_dim, int n_ff, int num_sms, int ntok);
-cudaError_t decode_launch(const DecPlan &plan, const DecArgs &A, int head_dim, cudaStream_t st);
+// A == nullptr: only check that the instance's CTA fits on an SM.
+cudaError_t decode_launch(const DecPlan &plan, const DecArgs *A, int head_dim, cudaStream_t st);
 constexpr int DEC_CHUNK = 16;  // attention chunk of the persistent kernel (positions)
 
 // Device error flag (timeouts in bounded waits).
