@@ -23,6 +23,7 @@
 #include <map>
 #include <memory>
 #include <string>
+#include <initializer_list>
 #include <unordered_map>
 #include <vector>
 
@@ -63,6 +64,8 @@ struct acm_engine {
     std::string err;
     void *scratch = nullptr;
     size_t scratch_bytes = 0;
+    void *scratch2 = nullptr;  // operand splits of acm_matmul_dev's tensor-core path
+    size_t scratch2_bytes = 0;
 };
 
 namespace {
@@ -74,6 +77,11 @@ struct DevTensor {
     int64_t numel = 0;
     size_t nbytes = 0;
     uint8_t *d = nullptr;
+    // bf16 hi/lo split of the dequantized weights for the tensor-core GEMM
+    // (built on first use; split_state 1 ready, -1 unavailable)
+    void *whi = nullptr, *wlo = nullptr;
+    TensorMap mhi, mlo;
+    int split_state = 0;
     int64_t k() const { return dims.empty() ? numel : (int64_t)dims[0]; }
     int64_t rows() const { return dims.size() < 2 ? 1 : numel / (int64_t)dims[0]; }
 };
@@ -134,6 +142,13 @@ struct acm_model {
     int tdec = 8;  // largest decode batch (max(8, max_seqs))
     float *x = nullptr, *h = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *hb = nullptr,
           *hb2 = nullptr, *part = nullptr, *logits = nullptr;
+
+    // tensor-core GEMM: activations split into bf16 hi/lo [T][kmax] and their
+    // tensor maps for K = n_embd, q_dim, n_ff
+    void *xs_hi = nullptr, *xs_lo = nullptr;
+    TensorMap xmap_hi[3], xmap_lo[3];
+    int xmap_k[3] = {0, 0, 0};
+    int mma_state = 0;  // 0 untried, 1 usable, -1 unavailable
 
     // per-token metadata and sampler state (device + pinned staging)
     int32_t *d_tok = nullptr, *d_seq = nullptr, *d_pos = nullptr, *d_out = nullptr, *d_topk = nullptr;
@@ -246,6 +261,72 @@ int attn_nsplit(acm_model *m, int ntok, int max_pos) {
 // One pass over `ntok` tokens whose ids/slots/positions are already in
 // d_tok/d_seq/d_pos.  Logits are produced for tokens [lm_first, lm_first +
 // lm_count) into their slots' rows of m->logits.  Enqueues only (capturable).
+// ---- tensor-core GEMM plumbing ----
+// The split cache of a weight tensor (exact dequant -> bf16 hi/lo), built on
+// first use.  False when the tensor cannot take the tensor-core path.
+bool ensure_split(acm_model *m, DevTensor *t) {
+    if (t->split_state) return t->split_state > 0;
+    t->split_state = -1;
+    const int64_t n = t->rows(), k = t->k();
+    if (k % 64 || n <= 0) return false;
+    if (dalloc(m, reinterpret_cast<uint16_t **>(&t->whi), (size_t)n * k) != cudaSuccess ||
+        dalloc(m, reinterpret_cast<uint16_t **>(&t->wlo), (size_t)n * k) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    if (split_weight_launch((int)t->type, t->d, n, (int)k, t->whi, t->wlo, m->e->stream) != cudaSuccess) return false;
+    if (!bf16_map(&t->mhi, t->whi, n, k) || !bf16_map(&t->mlo, t->wlo, n, k)) return false;
+    t->split_state = 1;
+    return true;
+}
+
+// Activation split buffers and their maps (once per model).
+bool mma_ready(acm_model *m) {
+    if (m->mma_state) return m->mma_state > 0;
+    m->mma_state = -1;
+    if (!mma_available()) return false;
+    const acm_config &c = m->c;
+    const int qd = c.n_head * c.head_dim;
+    const int ks[3] = {c.n_embd, qd, c.n_ff};
+    const int kmax = std::max(ks[0], std::max(ks[1], ks[2]));
+    const size_t T = (size_t)std::max(TMAX, m->tdec);
+    if (dalloc(m, reinterpret_cast<uint16_t **>(&m->xs_hi), T * kmax) != cudaSuccess ||
+        dalloc(m, reinterpret_cast<uint16_t **>(&m->xs_lo), T * kmax) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    for (int i = 0; i < 3; i++) {
+        if (ks[i] % 64) return false;
+        m->xmap_k[i] = ks[i];
+        if (!bf16_map(&m->xmap_hi[i], m->xs_hi, (int64_t)T, ks[i]) ||
+            !bf16_map(&m->xmap_lo[i], m->xs_lo, (int64_t)T, ks[i]))
+            return false;
+    }
+    m->mma_state = 1;
+    return true;
+}
+
+// Split fp32 activations x [ntok][k] into the model's bf16 buffers and
+// return the maps for this K (nullptr when the tensor-core path is off).
+int mma_split_x(acm_model *m, const float *x, int ldx, int ntok, int k, const TensorMap **hi, const TensorMap **lo) {
+    int i = 0;
+    while (i < 3 && m->xmap_k[i] != k) i++;
+    if (i == 3) return set_err(m, ACM_ERR_INVALID, "no activation map for this K");
+    CK_M(split_act_launch(x, ldx, ntok, k, m->xs_hi, m->xs_lo, m->e->stream));
+    *hi = &m->xmap_hi[i];
+    *lo = &m->xmap_lo[i];
+    return ACM_OK;
+}
+
+// Whether the tensor-core GEMM serves a GEMM of these weights (batches of
+// more than 8 tokens; exact split caches built here).
+bool use_mma(acm_model *m, std::initializer_list<DevTensor *> ts) {
+    if (!mma_ready(m)) return false;
+    for (DevTensor *t : ts)
+        if (t && !ensure_split(m, t)) return false;
+    return true;
+}
+
 // `decode`: every token belongs to a different sequence (one new token each),
 // which enables the fused decode attention; `amax`: fold the lm_head rows
 // into per-token argmax keys (greedy sampling) instead of only storing logits.
@@ -271,6 +352,14 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
                                  {L.k->d, nullptr, (int)L.k->type, kvd, EPI_STORE, m->k, kvd, L.k_b, nullptr},
                                  {L.v->d, nullptr, (int)L.v->type, kvd, EPI_STORE, m->v, kvd, L.v_b, nullptr}};
             CK_M(gemv_launch(sg, 3, m->x, E, E, ntok, L.attn_nw, eps, S, st));
+        } else if (use_mma(m, {L.q, L.k, L.v})) {
+            CK_M(rmsnorm_launch(m->x, E, L.attn_nw, m->h, E, ntok, E, eps, st));
+            const TensorMap *xh, *xl;
+            if (int rc = mma_split_x(m, m->h, E, ntok, E, &xh, &xl)) return rc;
+            MmaGemmSeg sg[3] = {{&L.q->mhi, &L.q->mlo, nullptr, nullptr, qd, EPI_STORE, m->q, qd, L.q_b, nullptr},
+                                {&L.k->mhi, &L.k->mlo, nullptr, nullptr, kvd, EPI_STORE, m->k, kvd, L.k_b, nullptr},
+                                {&L.v->mhi, &L.v->mlo, nullptr, nullptr, kvd, EPI_STORE, m->v, kvd, L.v_b, nullptr}};
+            CK_M(mma_gemm_launch(sg, 3, xh, xl, ntok, E, st));
         } else {
             CK_M(rmsnorm_launch(m->x, E, L.attn_nw, m->h, E, ntok, E, eps, st));
             CK_M(gemm_launch({L.q->d, nullptr, (int)L.q->type, qd, E, ntok, m->h, E, m->q, qd, EPI_STORE, L.q_b, nullptr}, st));
@@ -292,6 +381,11 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
         if (gemv_supported(L.o->type, qd, ntok)) {
             GemvSegDesc so{L.o->d, nullptr, (int)L.o->type, E, EPI_ADD, m->x, E, nullptr, nullptr};
             CK_M(gemv_launch(&so, 1, m->att, qd, qd, ntok, nullptr, eps, S, st));
+        } else if (use_mma(m, {L.o})) {
+            const TensorMap *xh, *xl;
+            if (int rc = mma_split_x(m, m->att, qd, ntok, qd, &xh, &xl)) return rc;
+            MmaGemmSeg so{&L.o->mhi, &L.o->mlo, nullptr, nullptr, E, EPI_ADD, m->x, E, nullptr, nullptr};
+            CK_M(mma_gemm_launch(&so, 1, xh, xl, ntok, qd, st));
         } else {
             CK_M(gemm_launch({L.o->d, nullptr, (int)L.o->type, E, qd, ntok, m->att, qd, m->x, E, EPI_ADD, nullptr, nullptr}, st));
         }
@@ -307,6 +401,13 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
                 CK_M(gemv_launch(sf, 2, m->x, E, E, ntok, L.ffn_nw, eps, S, st));
                 CK_M(swiglu_launch(m->hb, m->hb2, m->hb, (int64_t)ntok * F, st));
             }
+        } else if (use_mma(m, {L.gate, L.up}) && F % 64 == 0) {
+            // both projections split to bf16: one paired launch whatever their types
+            CK_M(rmsnorm_launch(m->x, E, L.ffn_nw, m->h, E, ntok, E, eps, st));
+            const TensorMap *xh, *xl;
+            if (int rc = mma_split_x(m, m->h, E, ntok, E, &xh, &xl)) return rc;
+            MmaGemmSeg sf{&L.gate->mhi, &L.gate->mlo, &L.up->mhi, &L.up->mlo, F, EPI_SWIGLU, m->hb, F, nullptr, nullptr};
+            CK_M(mma_gemm_launch(&sf, 1, xh, xl, ntok, E, st));
         } else {
             CK_M(rmsnorm_launch(m->x, E, L.ffn_nw, m->h, E, ntok, E, eps, st));
             if (pair) {
@@ -321,6 +422,11 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
         if (gemv_supported(L.down->type, F, ntok)) {
             GemvSegDesc sd{L.down->d, nullptr, (int)L.down->type, E, EPI_ADD, m->x, E, nullptr, nullptr};
             CK_M(gemv_launch(&sd, 1, m->hb, F, F, ntok, nullptr, eps, S, st));
+        } else if (use_mma(m, {L.down})) {
+            const TensorMap *xh, *xl;
+            if (int rc = mma_split_x(m, m->hb, F, ntok, F, &xh, &xl)) return rc;
+            MmaGemmSeg sd{&L.down->mhi, &L.down->mlo, nullptr, nullptr, E, EPI_ADD, m->x, E, nullptr, nullptr};
+            CK_M(mma_gemm_launch(&sd, 1, xh, xl, ntok, F, st));
         } else {
             CK_M(gemm_launch({L.down->d, nullptr, (int)L.down->type, E, F, ntok, m->hb, F, m->x, E, EPI_ADD, nullptr, nullptr}, st));
         }
@@ -333,6 +439,13 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
             GemvSegDesc so{m->out->d, nullptr, (int)m->out->type, V, EPI_STORE, m->logits, c.vocab, nullptr,
                            m->d_seq + lm_first, amax};
             CK_M(gemv_launch(&so, 1, xin, E, E, lm_count, m->out_nw, eps, S, st));
+        } else if (use_mma(m, {m->out})) {
+            CK_M(rmsnorm_launch(xin, E, m->out_nw, m->h, E, lm_count, E, eps, st));
+            const TensorMap *xh, *xl;
+            if (int rc = mma_split_x(m, m->h, E, lm_count, E, &xh, &xl)) return rc;
+            MmaGemmSeg sl{&m->out->mhi, &m->out->mlo, nullptr, nullptr, V, EPI_STORE, m->logits, c.vocab, nullptr,
+                          m->d_seq + lm_first};
+            CK_M(mma_gemm_launch(&sl, 1, xh, xl, lm_count, E, st));
         } else {
             CK_M(rmsnorm_launch(xin, E, m->out_nw, m->h, E, lm_count, E, eps, st));
             CK_M(gemm_launch({m->out->d, nullptr, (int)m->out->type, V, E, lm_count, m->h, E, m->logits, c.vocab,
@@ -497,11 +610,15 @@ int decode_graph_launch(acm_model *m, int ntok, bool greedy) {
         gr.kernels = captured;
         it = m->graphs.emplace(key, gr).first;
     }
+    // greedy batches whose lm_head runs as a matvec fold the argmax into its
+    // epilogue; larger batches (GEMM lm_head) take the greedy sampler pass
+    const bool fold = greedy && gemv_supported((int)m->out->type, m->c.n_embd, ntok);
+    unsigned long long *amax = fold ? m->d_amax : nullptr;
     if (it == m->graphs.end()) {
         // warm-up run outside capture (first launches set kernel attributes)
-        int rc = forward_pass(m, ntok, m->c.max_ctx - 1, 0, ntok, true, greedy ? m->d_amax : nullptr);
+        int rc = forward_pass(m, ntok, m->c.max_ctx - 1, 0, ntok, true, amax);
         if (rc) return rc;
-        if (!greedy && (rc = sample_pass(m, ntok, greedy))) return rc;
+        if (!fold && (rc = sample_pass(m, ntok, greedy))) return rc;
         CK_M(cudaMemsetAsync(m->d_amax, 0, sizeof(unsigned long long) * ntok, st));
         if ((rc = sync_check(m))) return rc;
         cudaGraph_t g = nullptr;
@@ -509,9 +626,9 @@ int decode_graph_launch(acm_model *m, int ntok, bool greedy) {
         CK_M(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
         // greedy: the lm_head epilogue keeps the argmax and advance reads it;
         // otherwise the top-k sampler runs between them
-        rc = forward_pass(m, ntok, m->c.max_ctx - 1, 0, ntok, true, greedy ? m->d_amax : nullptr);
-        if (!rc && !greedy) rc = sample_pass(m, ntok, greedy);
-        cudaError_t ae = advance_launch(m->d_tok, m->d_pos, m->d_step, m->d_out, greedy ? m->d_amax : nullptr,
+        rc = forward_pass(m, ntok, m->c.max_ctx - 1, 0, ntok, true, amax);
+        if (!rc && !fold) rc = sample_pass(m, ntok, greedy);
+        cudaError_t ae = advance_launch(m->d_tok, m->d_pos, m->d_step, m->d_out, amax,
                                         m->d_hist, HIST_MAX, m->d_hist_col, ntok, st);
         cudaError_t ce = cudaStreamEndCapture(st, &g);
         const unsigned long long captured = g_kernel_launches.load() - before;
@@ -614,6 +731,7 @@ ACM_API int acm_open(int device, acm_engine **out) {
 static void engine_free(acm_engine *e) {
     cudaSetDevice(e->device);
     if (e->scratch) cudaFree(e->scratch);
+    if (e->scratch2) cudaFree(e->scratch2);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
 }
@@ -624,10 +742,7 @@ ACM_API int acm_close(acm_engine *e) {
         e->closed = true;
         return ACM_OK;
     }
-    cudaSetDevice(e->device);
-    if (e->scratch) cudaFree(e->scratch);
-    if (e->stream) cudaStreamDestroy(e->stream);
-    delete e;
+    engine_free(e);
     return ACM_OK;
 }
 
@@ -1330,6 +1445,18 @@ static int scratch(acm_engine *e, size_t bytes, uint8_t **p) {
 
 static size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
 
+static int scratch2(acm_engine *e, size_t bytes, uint8_t **p) {
+    if (e->scratch2_bytes < bytes) {
+        if (e->scratch2) cudaFree(e->scratch2);
+        e->scratch2 = nullptr;
+        e->scratch2_bytes = 0;
+        CK_E(cudaMalloc(&e->scratch2, bytes));
+        e->scratch2_bytes = bytes;
+    }
+    *p = static_cast<uint8_t *>(e->scratch2);
+    return ACM_OK;
+}
+
 ACM_API int acm_dequant(acm_engine *e, uint32_t ggml_type, const void *host_bytes, int64_t nrows, int64_t k,
                         float *host_out) {
     if (!e || !host_bytes || !host_out || nrows <= 0 || k <= 0) return ACM_ERR_INVALID;
@@ -1359,6 +1486,20 @@ ACM_API int acm_matmul_dev(acm_engine *e, uint32_t ggml_type, const void *d_w, i
     if (gemv_supported((int)ggml_type, k, m)) {
         GemvSegDesc sg{d_w, nullptr, (int)ggml_type, n, EPI_STORE, d_y, (int)n, nullptr, nullptr};
         CK_E(gemv_launch(&sg, 1, d_x, (int)k, k, m, nullptr, 0.f, e->num_sms, e->stream));
+    } else if (k % 64 == 0 && mma_available()) {
+        // tensor-core path: split W and x to bf16 hi/lo in the second scratch
+        const size_t wbs = al256((size_t)n * k * 2), xbs = al256((size_t)m * k * 2);
+        uint8_t *s2 = nullptr;
+        if (int rc = scratch2(e, 2 * wbs + 2 * xbs, &s2)) return rc;
+        uint8_t *whi = s2, *wlo = s2 + wbs, *xhi = s2 + 2 * wbs, *xlo = xhi + xbs;
+        CK_E(split_weight_launch((int)ggml_type, d_w, n, (int)k, whi, wlo, e->stream));
+        CK_E(split_act_launch(d_x, (int)k, m, (int)k, xhi, xlo, e->stream));
+        TensorMap mwh, mwl, mxh, mxl;
+        if (!bf16_map(&mwh, whi, n, k) || !bf16_map(&mwl, wlo, n, k) || !bf16_map(&mxh, xhi, m, k) ||
+            !bf16_map(&mxl, xlo, m, k))
+            return set_eerr(e, ACM_ERR_CUDA, "tensor map encoding failed");
+        MmaGemmSeg sg{&mwh, &mwl, nullptr, nullptr, n, EPI_STORE, d_y, (int)n, nullptr, nullptr};
+        CK_E(mma_gemm_launch(&sg, 1, &mxh, &mxl, m, (int)k, e->stream));
     } else {
         CK_E(gemm_launch({d_w, nullptr, (int)ggml_type, n, k, m, d_x, (int)k, d_y, (int)n, EPI_STORE, nullptr, nullptr},
                          e->stream));

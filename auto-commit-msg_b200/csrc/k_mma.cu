@@ -1,0 +1,460 @@
+// k_mma.cu -- tensor-core GEMM for prefill (and batched decode):
+// y[m][n] (epi)= x[m][:] . W[n][:], the matmul of tensor.go:253-303 for M > 8
+// tokens, on the 5th-generation tensor cores.
+//
+// Precision.  The reference computes in fp32.  One bf16 product (8-bit
+// mantissa) gives ~1e-3 relative error on the logits, too coarse, so each
+// operand is split into a bf16 pair v = hi + lo (hi = bf16(v), lo = bf16(v -
+// hi)) and the product is formed as hi.hi + hi.lo + lo.hi with fp32
+// accumulation (the lo.lo term is below 2^-16 of the product): three MMAs per
+// K step, relative error ~1e-5.
+//
+// Layout.  Dequantization (exact, tensor.go:55-226) happens once per weight
+// tensor into two bf16 [n][K] arrays (the "split cache", 4 bytes per weight,
+// built on first use and kept in HBM); activations are split per call.  Both
+// are loaded by TMA into 128-byte-swizzled K-major tiles.
+//
+// Kernel.  One CTA computes a tile of 128 weight rows x 64 tokens (for a
+// SwiGLU pair: 64 gate rows + the same 64 up rows) over the whole K:
+//   warp 0 lane 0  TMA producer: 4-stage ring of (A hi, A lo, B hi, B lo),
+//                  64 K-elements per stage;
+//   warp 1         allocates 64 TMEM columns; lane 0 issues
+//                  tcgen05.mma (M=128, N=64, K=16, kind::f16, bf16 in, fp32
+//                  accumulate) and frees stages with tcgen05.commit;
+//   warps 2..5     epilogue: tcgen05.ld of their 32 TMEM lanes, bias,
+//                  store / residual add / SwiGLU, coalesced over rows.
+// Every wait is bounded; on a timeout the kernel records DEV_ERR_TIMEOUT,
+// waits (bounded) for its copies and MMAs in flight, frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "launch.cuh"
+#include "quant.cuh"
+
+namespace acm {
+
+namespace {
+
+constexpr int MBM = 128;  // weight rows per tile (MMA M)
+constexpr int MBN = 64;   // tokens per tile (MMA N)
+constexpr int MBK = 64;   // K elements per stage (128 bytes of bf16: one swizzle row)
+constexpr int MST = 4;    // stages
+constexpr int A_BYTES = MBM * MBK * 2;  // 16 KB
+constexpr int B_BYTES = MBN * MBK * 2;  // 8 KB
+constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+constexpr int MMA_THREADS = 192;
+constexpr int MMA_SMEM = MST * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t TMEM_COLS = 64;
+
+// ---- PTX wrappers ----
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, rows of 128
+// bytes in 8-row (1024-byte) atoms -- the layout TMA writes with
+// CU_TENSOR_MAP_SWIZZLE_128B and a 64-element bf16 box row.  Fields: start
+// address >> 4 [0,14), leading byte offset (1: unused for swizzled K-major)
+// [16,30), stride byte offset 1024 >> 4 [32,46), version 1 [46,48), layout
+// 2 = SWIZZLE_128B [61,64).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor, kind::f16: fp32 accumulator [4,6)=1, A and B bf16
+// [7,10)=1 [10,13)=1, both K-major, N >> 3 at [17,23), M >> 4 at [24,29).
+constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MBN >> 3) << 17) |
+                           ((uint32_t)(MBM >> 4) << 24);
+
+}  // namespace
+
+// One weight matrix (or SwiGLU pair) of a grouped launch.
+struct MmaSeg {
+    CUtensorMap ahi, alo;    // W split cache, box {64, 64 rows}
+    CUtensorMap ahi2, alo2;  // pair: the up-projection's cache
+    int n;                   // rows
+    int pair;
+    int tile0;               // first tile index of this segment
+    int epi;
+    float *y;
+    int ldy;
+    const float *bias;
+    const int32_t *yrow;
+};
+constexpr int MMA_MAX_SEG = 3;
+struct MmaArgs {
+    MmaSeg seg[MMA_MAX_SEG];
+    int nseg;
+    CUtensorMap bhi, blo;  // activations split, box {64, 64 rows}
+    int m, k;
+    int ttiles;            // token tiles
+};
+
+__global__ void __launch_bounds__(MMA_THREADS, 1) k_mma_gemm(const __grid_constant__ MmaArgs A) {
+    extern __shared__ uint8_t msm_raw[];
+    uint8_t *msm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(msm_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(msm + MST * STAGE_BYTES);
+    uint64_t *empty = full + MST;
+    uint64_t *accf = empty + MST;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accf + 1);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    // tile -> (segment, row tile, token tile); token tiles fastest so CTAs
+    // sharing a weight tile run together (L2 reuse)
+    int si = 0;
+    while (si + 1 < A.nseg && (int)blockIdx.x >= A.seg[si + 1].tile0) si++;
+    const MmaSeg &S = A.seg[si];
+    const int local = blockIdx.x - S.tile0;
+    const int rt = local / A.ttiles, tt = local - rt * A.ttiles;
+    const int rows_per_tile = S.pair ? MBM / 2 : MBM;
+    const int row0 = rt * rows_per_tile, tok0 = tt * MBN;
+    const int KT = A.k / MBK;
+
+    if (tid == 0) {
+        for (int i = 0; i < MST; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(accf, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_wait();
+    if (tid == 0) pdl_trigger();
+
+    if (warp == 0 && lane == 0) {
+        // ---- TMA producer ----
+        int issued = 0;
+        for (int kt = 0; kt < KT; kt++) {
+            const int s = kt % MST;
+            if (kt >= MST && !mbar_wait(&empty[s], ((kt / MST) & 1) ^ 1)) break;
+            uint8_t *st = msm + s * STAGE_BYTES;
+            mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+            const int kx = kt * MBK;
+            if (S.pair) {
+                tma_load_2d(st, &S.ahi, kx, row0, &full[s]);
+                tma_load_2d(st + A_BYTES / 2, &S.ahi2, kx, row0, &full[s]);
+                tma_load_2d(st + A_BYTES, &S.alo, kx, row0, &full[s]);
+                tma_load_2d(st + A_BYTES + A_BYTES / 2, &S.alo2, kx, row0, &full[s]);
+            } else {
+                tma_load_2d(st, &S.ahi, kx, row0, &full[s]);
+                tma_load_2d(st + A_BYTES / 2, &S.ahi, kx, row0 + 64, &full[s]);
+                tma_load_2d(st + A_BYTES, &S.alo, kx, row0, &full[s]);
+                tma_load_2d(st + A_BYTES + A_BYTES / 2, &S.alo, kx, row0 + 64, &full[s]);
+            }
+            tma_load_2d(st + 2 * A_BYTES, &A.bhi, kx, tok0, &full[s]);
+            tma_load_2d(st + 2 * A_BYTES + B_BYTES, &A.blo, kx, tok0, &full[s]);
+            issued = kt + 1;
+        }
+        // no copy may still be landing when the CTA exits: wait (bounded)
+        // for the last fill of every stage used
+        for (int s = 0; s < MST && s < issued; s++) {
+            const int last = s + ((issued - 1 - s) / MST) * MST;  // last kt that used stage s
+            mbar_wait(&full[s], (last / MST) & 1);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer ----
+        for (int kt = 0; kt < KT; kt++) {
+            const int s = kt % MST;
+            if (!mbar_wait(&full[s], (kt / MST) & 1)) break;
+            tc_fence_after();
+            const uint32_t st = smem_u32(msm + s * STAGE_BYTES);
+            const uint32_t ahi = st, alo = st + A_BYTES, bhi = st + 2 * A_BYTES, blo = bhi + B_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < MBK / 16; kk++) {
+                const uint32_t off = kk * 32;  // 16 bf16 along K inside the swizzled row
+                const uint64_t dah = sw128_desc(ahi + off), dal = sw128_desc(alo + off);
+                const uint64_t dbh = sw128_desc(bhi + off), dbl = sw128_desc(blo + off);
+                tc_mma(tmem, dah, dbh, IDESC, (kt | kk) != 0);
+                tc_mma(tmem, dah, dbl, IDESC, 1u);
+                tc_mma(tmem, dal, dbh, IDESC, 1u);
+            }
+            tc_commit(&empty[s]);  // stage free once these MMAs have read it
+        }
+        tc_commit(accf);  // all MMAs issued so far complete -> accumulator ready
+    } else if (warp >= 2) {
+        // ---- epilogue ----
+        const int q = warp & 3;  // TMEM lane quadrant this warp may access
+        const bool ok = mbar_wait(accf, 0);
+        tc_fence_after();
+        if (ok) {
+            const int lrow = q * 32 + lane;  // accumulator row (TMEM lane)
+            float *xch = reinterpret_cast<float *>(msm);  // pair exchange [64][MBN + 1]
+            for (int c0 = 0; c0 < MBN; c0 += 16) {
+                float v[16];
+                tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+                if (S.pair) {
+                    // lanes 64..127 hold the up rows: hand them to the gate warps
+                    if (q >= 2)
+#pragma unroll
+                        for (int j = 0; j < 16; j++) xch[(lrow - 64) * (MBN + 1) + c0 + j] = v[j];
+                    named_sync(1, 128);
+                    if (q < 2) {
+                        const int n = row0 + lrow;
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            const int tok = tok0 + c0 + j;
+                            if (n < S.n && tok < A.m) {
+                                const float g = v[j], u = xch[lrow * (MBN + 1) + c0 + j];
+                                const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, fast_exp(-g)));
+                                float *yp = S.y + (int64_t)(S.yrow ? S.yrow[tok] : tok) * S.ldy + n;
+                                *yp = __fmul_rn(__fmul_rn(g, sg), u);
+                            }
+                        }
+                    }
+                    named_sync(1, 128);
+                } else {
+                    const int n = row0 + lrow;
+                    if (n < S.n) {
+                        const float b = S.bias ? S.bias[n] : 0.f;
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            const int tok = tok0 + c0 + j;
+                            if (tok < A.m) {
+                                float *yp = S.y + (int64_t)(S.yrow ? S.yrow[tok] : tok) * S.ldy + n;
+                                const float val = S.bias ? v[j] + b : v[j];
+                                if (S.epi == EPI_ADD) *yp = *yp + val;
+                                else *yp = val;
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        // the accumulator must be idle before it is freed (immediate unless a
+        // wait above ran out)
+        mbar_wait(accf, 0);
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Operand preparation
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void split_bf16(float v, __nv_bfloat16 &hi, __nv_bfloat16 &lo) {
+    hi = __float2bfloat16_rn(v);
+    lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+}
+
+// x[m][ldx] fp32 -> hi, lo [m][k] bf16
+__global__ void k_split_act(const float *x, int ldx, int m, int k, __nv_bfloat16 *hi, __nv_bfloat16 *lo) {
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
+    const int64_t total = (int64_t)m * k / 4;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t e = i * 4;
+        const int r = (int)(e / k), c = (int)(e - (int64_t)r * k);
+        const float4 v = *reinterpret_cast<const float4 *>(x + (int64_t)r * ldx + c);
+        __nv_bfloat16 h[4], l[4];
+        split_bf16(v.x, h[0], l[0]);
+        split_bf16(v.y, h[1], l[1]);
+        split_bf16(v.z, h[2], l[2]);
+        split_bf16(v.w, h[3], l[3]);
+        *reinterpret_cast<uint2 *>(hi + e) = *reinterpret_cast<uint2 *>(h);
+        *reinterpret_cast<uint2 *>(lo + e) = *reinterpret_cast<uint2 *>(l);
+    }
+}
+
+// Exact dequantization of W [n][k] (ggml blocks) -> hi, lo [n][k] bf16.
+template <int T>
+__global__ void k_split_weight(const uint8_t *w, int64_t n, int k, __nv_bfloat16 *hi, __nv_bfloat16 *lo) {
+    const int64_t rb = row_bytes(T, k);
+    const int runs = k / 32;
+    const int64_t total = n * runs;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / runs;
+        const int run = (int)(i - r * runs);
+        float v[32];
+        dequant_run32<T>(w + r * rb, run, v);
+        __nv_bfloat16 h[32], l[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) split_bf16(v[j], h[j], l[j]);
+        uint4 *ph = reinterpret_cast<uint4 *>(hi + r * k + run * 32);
+        uint4 *pl = reinterpret_cast<uint4 *>(lo + r * k + run * 32);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            ph[j] = reinterpret_cast<const uint4 *>(h)[j];
+            pl[j] = reinterpret_cast<const uint4 *>(l)[j];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool encode_fn() {
+    std::call_once(g_encode_once, [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    return g_encode != nullptr;
+}
+}  // namespace
+
+bool mma_available() {
+    static int avail = -1;
+    if (avail < 0) {
+        int dev = 0, major = 0, minor = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+        avail = (major == 10 && minor == 0 && encode_fn()) ? 1 : 0;
+        const char *e = getenv("ACM_MMA");
+        if (e && e[0] == '0') avail = 0;
+    }
+    return avail == 1;
+}
+
+// 2-D bf16 map over [rows][k] (row stride k elements), box {64, 64 rows},
+// 128-byte swizzle; rows beyond `rows` read as zero.
+static_assert(sizeof(TensorMap) == sizeof(CUtensorMap), "tensor map storage");
+bool bf16_map(TensorMap *tmap, const void *base, int64_t rows, int64_t k) {
+    CUtensorMap *map = reinterpret_cast<CUtensorMap *>(tmap);
+    if (!encode_fn() || k % MBK || ((uintptr_t)base & 15)) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+    cuuint32_t box[2] = {MBK, 64};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+cudaError_t split_act_launch(const float *x, int ldx, int m, int k, void *hi, void *lo, cudaStream_t st) {
+    if (m <= 0) return cudaSuccess;
+    if (k % 4 || ldx % 4) return cudaErrorInvalidValue;
+    const int64_t total = (int64_t)m * k / 4;
+    const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
+    cudaError_t e = launch_pdl(k_split_act, dim3(grid), dim3(256), 0, st, x, ldx, m, k,
+                               static_cast<__nv_bfloat16 *>(hi), static_cast<__nv_bfloat16 *>(lo));
+    if (e != cudaSuccess) return e;
+    return launched(1);
+}
+
+cudaError_t split_weight_launch(int type, const void *w, int64_t n, int k, void *hi, void *lo, cudaStream_t st) {
+    if (k % 32) return cudaErrorInvalidValue;
+    const int64_t total = n * (k / 32);
+    const int grid = (int)std::min<int64_t>((total + 127) / 128, 148 * 16);
+    auto *h = static_cast<__nv_bfloat16 *>(hi);
+    auto *l = static_cast<__nv_bfloat16 *>(lo);
+    const uint8_t *wb = static_cast<const uint8_t *>(w);
+    switch (type) {
+        case T_F32: k_split_weight<T_F32><<<grid, 128, 0, st>>>(wb, n, k, h, l); break;
+        case T_F16: k_split_weight<T_F16><<<grid, 128, 0, st>>>(wb, n, k, h, l); break;
+        case T_Q4_0: k_split_weight<T_Q4_0><<<grid, 128, 0, st>>>(wb, n, k, h, l); break;
+        case T_Q5_0: k_split_weight<T_Q5_0><<<grid, 128, 0, st>>>(wb, n, k, h, l); break;
+        case T_Q8_0: k_split_weight<T_Q8_0><<<grid, 128, 0, st>>>(wb, n, k, h, l); break;
+        case T_Q4_K: k_split_weight<T_Q4_K><<<grid, 128, 0, st>>>(wb, n, k, h, l); break;
+        case T_Q5_K: k_split_weight<T_Q5_K><<<grid, 128, 0, st>>>(wb, n, k, h, l); break;
+        case T_Q6_K: k_split_weight<T_Q6_K><<<grid, 128, 0, st>>>(wb, n, k, h, l); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return launched(1);
+}
+
+cudaError_t mma_gemm_launch(const MmaGemmSeg *segs, int nseg, const TensorMap *x_hi, const TensorMap *x_lo, int m,
+                            int k, cudaStream_t st) {
+    if (nseg < 1 || nseg > MMA_MAX_SEG || m <= 0 || k % MBK) return cudaErrorInvalidValue;
+    MmaArgs a;
+    memset(&a, 0, sizeof(a));
+    a.nseg = nseg;
+    a.m = m;
+    a.k = k;
+    a.ttiles = (m + MBN - 1) / MBN;
+    a.bhi = *reinterpret_cast<const CUtensorMap *>(x_hi);
+    a.blo = *reinterpret_cast<const CUtensorMap *>(x_lo);
+    int tiles = 0;
+    for (int i = 0; i < nseg; i++) {
+        const MmaGemmSeg &g = segs[i];
+        MmaSeg &s = a.seg[i];
+        s.ahi = *reinterpret_cast<const CUtensorMap *>(g.map_hi);
+        s.alo = *reinterpret_cast<const CUtensorMap *>(g.map_lo);
+        s.pair = g.map_hi2 != nullptr;
+        if (s.pair) {
+            s.ahi2 = *reinterpret_cast<const CUtensorMap *>(g.map_hi2);
+            s.alo2 = *reinterpret_cast<const CUtensorMap *>(g.map_lo2);
+        }
+        s.n = (int)g.n;
+        s.epi = g.epi;
+        s.y = g.y;
+        s.ldy = g.ldy;
+        s.bias = g.bias;
+        s.yrow = g.yrow;
+        s.tile0 = tiles;
+        const int rpt = s.pair ? MBM / 2 : MBM;
+        tiles += (int)((g.n + rpt - 1) / rpt) * a.ttiles;
+    }
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev & 63]) {
+        cudaError_t e = cudaFuncSetAttribute(k_mma_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, MMA_SMEM);
+        if (e != cudaSuccess) return e;
+        attr[dev & 63] = true;
+    }
+    cudaError_t e = launch_pdl(k_mma_gemm, dim3(tiles), dim3(MMA_THREADS), MMA_SMEM, st, a);
+    if (e != cudaSuccess) return e;
+    return launched(1);
+}
+
+}  // namespace acm

@@ -88,6 +88,32 @@ struct GemmDesc {
 };
 cudaError_t gemm_launch(const GemmDesc &d, cudaStream_t st);
 
+// ---------------------------------------------------------------------------
+// Tensor-core GEMM (k_mma.cu): bf16 hi/lo split operands, three tcgen05 MMAs
+// per K step, fp32 accumulation in TMEM.
+struct alignas(64) TensorMap {
+    uint64_t w[16];  // CUtensorMap
+};
+bool mma_available();
+// 2-D bf16 tensor map over [rows][k] for the GEMM's 64x64 boxes.
+bool bf16_map(TensorMap *map, const void *base, int64_t rows, int64_t k);
+// fp32 [m][ldx] -> bf16 hi, lo [m][k]
+cudaError_t split_act_launch(const float *x, int ldx, int m, int k, void *hi, void *lo, cudaStream_t st);
+// exact dequant of W [n][k] -> bf16 hi, lo [n][k]
+cudaError_t split_weight_launch(int type, const void *w, int64_t n, int k, void *hi, void *lo, cudaStream_t st);
+struct MmaGemmSeg {
+    const TensorMap *map_hi, *map_lo;    // W split cache
+    const TensorMap *map_hi2, *map_lo2;  // SwiGLU pair: up-projection (else null)
+    int64_t n;                           // rows (a multiple of 64 for pairs)
+    int epi;
+    float *y;
+    int ldy;
+    const float *bias;
+    const int32_t *yrow;
+};
+cudaError_t mma_gemm_launch(const MmaGemmSeg *segs, int nseg, const TensorMap *x_hi, const TensorMap *x_lo, int m,
+                            int k, cudaStream_t st);
+
 // Dequantize rows (exact): rows either consecutive (row_ids == nullptr) or
 // gathered by id (embedding lookup, model.go:338-340).
 cudaError_t dequant_launch(int type, const void *w, int64_t k, int64_t nrows, const int32_t *row_ids,

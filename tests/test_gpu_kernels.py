@@ -2,10 +2,15 @@
 acm_sample_logits) against the CPU oracle.
 
 Tolerances: dequant bit-exact (tensor.go:55-226 is exact in fp32; the
-reference pins asm vs scalar at 0 difference, cmp_test.go:37-40); matmul
-relative L2 <= 2e-6 against a float64 product of the exact dequantized
-weights (fp32 accumulation in a different order); sampler ids identical.
+reference pins asm vs scalar at 0 difference, cmp_test.go:37-40); matvec
+(m <= 8, CUDA-core fp32) relative L2 <= 2e-6 against a float64 product of the
+exact dequantized weights (fp32 accumulation in a different order); GEMM
+(m > 8, K a multiple of 64) on the tensor cores with bf16 hi/lo split
+operands (hi.hi + hi.lo + lo.hi, fp32 accumulation) relative L2 <= 3e-5;
+GEMM with K not a multiple of 64 (CUDA-core fp32) 2e-6; sampler ids identical.
 """
+
+MMA_TOL = 3e-5  # tensor-core GEMM: bf16 split operands (three products)
 import os
 
 import numpy as np
@@ -70,7 +75,22 @@ def test_gemv_shapes(eng, oracle, synth, typ, n, k):
 @pytest.mark.parametrize("typ", list(TYPES.values()))
 @pytest.mark.parametrize("m", [9, 64, 130])
 def test_gemm(eng, oracle, synth, typ, m):
-    _check_matmul(eng, oracle, synth, typ, 200, 512, m, seed=typ * 3 + m)
+    _check_matmul(eng, oracle, synth, typ, 200, 512, m, seed=typ * 3 + m, tol=MMA_TOL)
+
+
+@pytest.mark.parametrize("typ", [12, 14])
+@pytest.mark.parametrize("shape", [(1024, 2048), (2048, 1024), (1024, 3072), (3072, 1024)])
+def test_gemm_prefill_shapes(eng, oracle, synth, typ, shape):
+    """The prefill GEMMs of the Qwen3-0.6B shape at a 389-token prompt
+    (ragged last token tile) on the tensor cores."""
+    k, n = shape
+    _check_matmul(eng, oracle, synth, typ, n, k, 389, seed=k + n + typ, tol=MMA_TOL)
+
+
+@pytest.mark.parametrize("typ", [0, 1, 2, 6, 8])
+def test_gemm_k_not_64(eng, oracle, synth, typ):
+    """K = 1056 (a multiple of 32, not of 64): the CUDA-core GEMM."""
+    _check_matmul(eng, oracle, synth, typ, 150, 1056, 40, seed=typ + 77)
 
 
 @pytest.mark.parametrize("typ", QTYPES)
