@@ -45,6 +45,11 @@ class CStats(C.Structure):
                 ("decode_s", C.c_double)]
 
 
+class CRequest(C.Structure):
+    _fields_ = [("prompt", C.c_void_p), ("n_prompt", C.c_int32), ("sampler", CSampler), ("max_tok", C.c_int32),
+                ("out_ids", C.c_void_p), ("n_out", C.c_int32), ("status", C.c_int32)]
+
+
 # name -> (restype, argtypes); every symbol of include/acm.h
 P = C.c_void_p
 SIGNATURES = {
@@ -79,6 +84,7 @@ SIGNATURES = {
     "acm_engine_sync": (C.c_int, [P]),
     "acm_model_last_timing": (C.c_int, [P, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "acm_kernel_launches": (C.c_uint64, []),
+    "acm_serve": (C.c_int, [P, C.POINTER(CRequest), C.c_int32, C.c_int32, C.c_int32, C.POINTER(CStats)]),
     "acm_model_trace": (C.c_int, [P, C.c_int32]),
     "acm_model_trace_read": (C.c_int, [P, P, C.c_int64, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
     "acm_model_bench_gemv": (C.c_int, [P, C.c_int32, C.POINTER(C.c_double), C.POINTER(C.c_double),

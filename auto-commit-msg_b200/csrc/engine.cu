@@ -1296,6 +1296,150 @@ ACM_API int acm_generate(acm_model *m, int32_t seq, const int32_t *prompt, int32
     return ACM_OK;
 }
 
+// Continuous batching over independent requests (no reference counterpart:
+// the reference serves one prompt per process).  Each request follows
+// Generate's loop (sampler.go:108-157) exactly as acm_generate does -- id_0
+// from the prefill logits with draw 0, then Forward + Sample with draw n + 1
+// -- while up to max_batch of them share each decode step.
+ACM_API int acm_serve(acm_model *m, acm_request *reqs, int32_t n, int32_t max_batch, int32_t stop_on_eos,
+                      acm_stats *stats) {
+    if (!m || !m->finalized) return set_err(m, ACM_ERR_INVALID, "model not finalized");
+    if (n < 0 || (n > 0 && !reqs)) return set_err(m, ACM_ERR_INVALID, "bad request list");
+    for (int i = 0; i < n; i++)
+        if (reqs[i].n_prompt < 0 || (reqs[i].n_prompt > 0 && !reqs[i].prompt) ||
+            (reqs[i].max_tok > 0 && !reqs[i].out_ids))
+            return set_err(m, ACM_ERR_INVALID, fmt("bad request %d", i));
+    cudaSetDevice(m->e->device);
+    const int B = std::max(1, std::min(max_batch > 0 ? max_batch : m->tdec, m->tdec));
+    cudaStream_t stream = m->e->stream;
+    const int64_t erows = m->embd->rows();
+    struct Act {
+        int r, seq;
+        int32_t id;
+    };
+    std::vector<Act> act;
+    acm_stats st{0, 0, 0, 0};
+    for (int i = 0; i < n; i++) {
+        reqs[i].n_out = 0;
+        reqs[i].status = ACM_OK;
+    }
+    auto is_stop = [&](int32_t id) { return stop_on_eos && (id == m->c.eos || id == m->c.eos2); };
+    int next = 0, rc = ACM_OK;
+    std::vector<int32_t> seqs, toks, outs;
+    std::vector<acm_sampler> sams;
+    std::vector<uint64_t> steps;
+    while (next < n || !act.empty()) {
+        // ---- admission: prefill new requests into free slots ----
+        std::vector<Act> fresh;
+        while ((int)(act.size() + fresh.size()) < B && next < n) {
+            acm_request &q = reqs[next];
+            int32_t seq = -1;
+            if (acm_seq_open(m, &seq) != ACM_OK) {
+                if (act.empty() && fresh.empty()) return set_err(m, ACM_ERR_INVALID, "no free sequence slot");
+                break;  // retry once a slot frees up
+            }
+            const int r = next++;
+            Seq &sq = m->seqs[seq];
+            int qrc = ACM_OK;
+            for (int i = 0; i < q.n_prompt && !qrc; i++)
+                if (q.prompt[i] < 0 || q.prompt[i] >= erows) qrc = set_err(m, ACM_ERR_INVALID, fmt("token id %d out of range", q.prompt[i]));
+            const int chunk = std::max(1, std::min(TMAX, m->c.max_ctx));
+            for (int i = 0; i < q.n_prompt && !qrc; i += chunk) {
+                const int end = std::min(i + chunk, q.n_prompt);
+                if (sq.pos + (end - i) > m->c.max_ctx) {
+                    qrc = set_err(m, ACM_ERR_CTX_EXCEEDED,
+                                  fmt("context length exceeded (%d > %d)", sq.pos + end - i, m->c.max_ctx));
+                    break;
+                }
+                CK_M(cudaEventRecord(m->ev[0], stream));
+                if ((rc = forward_seq(m, seq, q.prompt + i, end - i))) return rc;
+                CK_M(cudaEventRecord(m->ev[1], stream));
+                if ((rc = sync_check(m))) return rc;
+                st.prefill_s += ev_seconds(m->ev[0], m->ev[1]);
+                st.prefill_toks += end - i;
+            }
+            if (qrc || q.n_prompt == 0 || q.max_tok <= 0) {
+                q.status = qrc;
+                acm_seq_close(m, seq);
+                continue;
+            }
+            fresh.push_back(Act{r, seq, 0});
+        }
+        if (!fresh.empty()) {
+            // id_0 of every new request from its prefill logits (draw 0)
+            const int k = (int)fresh.size();
+            bool greedy = true;
+            for (int i = 0; i < k; i++) {
+                m->h_seq.p[i] = fresh[i].seq;
+                fill_sampler(m, i, &reqs[fresh[i].r].sampler, 0);
+                if (reqs[fresh[i].r].sampler.temp > 0) greedy = false;
+            }
+            CK_M(cudaMemcpyAsync(m->d_seq, m->h_seq.p, sizeof(int32_t) * k, cudaMemcpyHostToDevice, stream));
+            if ((rc = upload_sampler(m, k))) return rc;
+            if ((rc = sample_pass(m, k, greedy))) return rc;
+            CK_M(cudaMemcpyAsync(m->h_out.p, m->d_out, sizeof(int32_t) * k, cudaMemcpyDeviceToHost, stream));
+            if ((rc = sync_check(m))) return rc;
+            for (int i = 0; i < k; i++) {
+                fresh[i].id = m->h_out.p[i];
+                act.push_back(fresh[i]);
+            }
+        }
+        // ---- retire: stop id sampled, or no room for another position ----
+        for (size_t i = 0; i < act.size();) {
+            acm_request &q = reqs[act[i].r];
+            bool done = is_stop(act[i].id);
+            if (!done && m->seqs[act[i].seq].pos + 1 > m->c.max_ctx) {
+                q.out_ids[q.n_out++] = act[i].id;  // appended, then Forward fails (as acm_generate)
+                q.status = ACM_ERR_CTX_EXCEEDED;
+                done = true;
+            }
+            if (done) {
+                acm_seq_close(m, act[i].seq);
+                act[i] = act.back();
+                act.pop_back();
+            } else {
+                i++;
+            }
+        }
+        if (act.empty()) continue;
+        // ---- one batched decode step: Forward(id) + Sample with draw n + 1 ----
+        const int na = (int)act.size();
+        seqs.resize(na);
+        toks.resize(na);
+        outs.resize(na);
+        sams.resize(na);
+        steps.resize(na);
+        for (int i = 0; i < na; i++) {
+            const acm_request &q = reqs[act[i].r];
+            seqs[i] = act[i].seq;
+            toks[i] = act[i].id;
+            sams[i] = q.sampler;
+            steps[i] = (uint64_t)q.n_out + 1;
+        }
+        if ((rc = acm_decode_step(m, na, seqs.data(), toks.data(), sams.data(), steps.data(), outs.data(), nullptr)))
+            return rc;
+        st.decode_s += m->last_decode_s;
+        st.decode_toks += na;
+        for (size_t i = 0; i < act.size();) {
+            acm_request &q = reqs[act[i].r];
+            q.out_ids[q.n_out++] = act[i].id;
+            act[i].id = outs[i];
+            if (q.n_out >= q.max_tok) {
+                acm_seq_close(m, act[i].seq);
+                act[i] = act.back();
+                outs[i] = outs[act.size() - 1];
+                act.pop_back();
+            } else {
+                i++;
+            }
+        }
+    }
+    m->last_prefill_s = st.prefill_s;
+    m->last_decode_s = st.decode_s;
+    if (stats) *stats = st;
+    return ACM_OK;
+}
+
 ACM_API int32_t acm_max_logit(const float *logits, int32_t n) {
     int32_t best = 0;
     for (int32_t i = 1; i < n; i++)

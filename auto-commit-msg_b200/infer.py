@@ -189,6 +189,28 @@ class Model:
                 onToken(i)
         return ids
 
+    def Serve(self, requests: Sequence[tuple], max_batch: int = 0, stop_on_eos: bool = True):
+        """Continuous batching over independent requests (acm_serve): each
+        request is (prompt, Sampler, maxTok) and runs Generate's loop with the
+        same draws as Generate; up to max_batch (0: all free slots) share each
+        decode step.  Returns [(ids, status)] in request order; Stats holds
+        the summed prefill / decode tokens and device seconds."""
+        keep, reqs = [], (_lib.CRequest * max(len(requests), 1))()
+        for i, (prompt, s, max_tok) in enumerate(requests):
+            p = np.ascontiguousarray(prompt, dtype=np.int32)
+            out = np.zeros(max(int(max_tok), 1), dtype=np.int32)
+            keep.append((p, out))
+            reqs[i].prompt = p.ctypes.data
+            reqs[i].n_prompt = len(p)
+            reqs[i].sampler = (s or Sampler()).c()
+            reqs[i].max_tok = int(max_tok)
+            reqs[i].out_ids = out.ctypes.data
+        st = CStats()
+        self._check(_lib.lib().acm_serve(self._h, reqs, len(requests), int(max_batch), int(stop_on_eos),
+                                         C.byref(st)))
+        self.Stats = Stats(st.prefill_toks, st.prefill_s, st.decode_toks, st.decode_s)
+        return [([int(v) for v in keep[i][1][:reqs[i].n_out]], int(reqs[i].status)) for i in range(len(requests))]
+
     # -- batched decode (several sequence slots) --
     def open_seq(self) -> int:
         s = C.c_int32(-1)

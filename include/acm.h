@@ -97,7 +97,8 @@ ACM_API const char *acm_engine_error(acm_engine *e);
 ACM_API int acm_model_create(acm_engine *e, const acm_config *cfg, int32_t max_seqs, acm_model **out);
 
 /* Copy one GGUF tensor's bytes UNCHANGED to HBM (the blocks stay in ggml
- * layout; the model never holds a dequantized copy).  dims[0] is the
+ * layout and the decode matvecs read them as they are; the tensor-core GEMM
+ * of prefill builds a bf16 hi/lo copy of a linear weight on first use).  dims[0] is the
  * innermost dimension as in gguf.Tensor.Dims (gguf.go:42-49).  host_bytes may
  * point into an mmap and is not retained. */
 ACM_API int acm_model_add_tensor(acm_model *m, const char *name, uint32_t ggml_type, const uint64_t *dims,
@@ -152,6 +153,28 @@ ACM_API int acm_decode_step(acm_model *m, int32_t nseq, const int32_t *seqs, con
 ACM_API int acm_generate(acm_model *m, int32_t seq, const int32_t *prompt, int32_t n_prompt,
                          const acm_sampler *s, int32_t max_tok, int32_t stop_on_eos, int32_t *out_ids,
                          int32_t *n_out, acm_stats *stats);
+
+/* One request of acm_serve: a prompt and its sampler; out_ids (max_tok
+ * entries) receives the generated ids, n_out their count, status ACM_OK or
+ * the request's own error (ACM_ERR_CTX_EXCEEDED, ACM_ERR_INVALID). */
+typedef struct acm_request {
+    const int32_t *prompt;
+    int32_t n_prompt;
+    acm_sampler sampler;
+    int32_t max_tok;
+    int32_t *out_ids;
+    int32_t n_out;
+    int32_t status;
+} acm_request;
+
+/* Continuous batching, no reference counterpart (the reference serves one
+ * prompt per process): runs every request through Generate's loop
+ * (sampler.go:108-157, the same draws as acm_generate) with up to max_batch
+ * of them (<= the model's sequence slots) sharing each decode step; new
+ * requests are prefilled into slots as others finish.  stats: prefill and
+ * decode tokens and device seconds summed over all requests. */
+ACM_API int acm_serve(acm_model *m, acm_request *reqs, int32_t n, int32_t max_batch, int32_t stop_on_eos,
+                      acm_stats *stats);
 
 /* MaxLogit, model.go:462-471 (host helper, first maximum wins). */
 ACM_API int32_t acm_max_logit(const float *logits, int32_t n);
