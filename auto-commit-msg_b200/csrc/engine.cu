@@ -269,8 +269,8 @@ bool ensure_split(acm_model *m, DevTensor *t) {
     t->split_state = -1;
     const int64_t n = t->rows(), k = t->k();
     if (k % 64 || n <= 0) return false;
-    if (dalloc(m, reinterpret_cast<uint16_t **>(&t->whi), (size_t)n * k) != cudaSuccess ||
-        dalloc(m, reinterpret_cast<uint16_t **>(&t->wlo), (size_t)n * k) != cudaSuccess) {
+    if (dalloc(m, reinterpret_cast<uint16_t **>(&t->whi), (size_t)rows64(n) * k) != cudaSuccess ||
+        dalloc(m, reinterpret_cast<uint16_t **>(&t->wlo), (size_t)rows64(n) * k) != cudaSuccess) {
         cudaGetLastError();
         return false;
     }
@@ -289,7 +289,7 @@ bool mma_ready(acm_model *m) {
     const int qd = c.n_head * c.head_dim;
     const int ks[3] = {c.n_embd, qd, c.n_ff};
     const int kmax = std::max(ks[0], std::max(ks[1], ks[2]));
-    const size_t T = (size_t)std::max(TMAX, m->tdec);
+    const size_t T = (size_t)rows64(std::max(TMAX, m->tdec));
     if (dalloc(m, reinterpret_cast<uint16_t **>(&m->xs_hi), T * kmax) != cudaSuccess ||
         dalloc(m, reinterpret_cast<uint16_t **>(&m->xs_lo), T * kmax) != cudaSuccess) {
         cudaGetLastError();
@@ -1632,7 +1632,7 @@ ACM_API int acm_matmul_dev(acm_engine *e, uint32_t ggml_type, const void *d_w, i
         CK_E(gemv_launch(&sg, 1, d_x, (int)k, k, m, nullptr, 0.f, e->num_sms, e->stream));
     } else if (k % 64 == 0 && mma_available()) {
         // tensor-core path: split W and x to bf16 hi/lo in the second scratch
-        const size_t wbs = al256((size_t)n * k * 2), xbs = al256((size_t)m * k * 2);
+        const size_t wbs = al256((size_t)rows64(n) * k * 2), xbs = al256((size_t)rows64(m) * k * 2);
         uint8_t *s2 = nullptr;
         if (int rc = scratch2(e, 2 * wbs + 2 * xbs, &s2)) return rc;
         uint8_t *whi = s2, *wlo = s2 + wbs, *xhi = s2 + 2 * wbs, *xlo = xhi + xbs;

@@ -44,9 +44,9 @@ __device__ __forceinline__ int x_off(int k, int K, bool wide) {
 // into the x area.  The activations were written by other CTAs an instant
 // ago, so each thread issues all of its loads (XB per token at a time, with
 // the norm weights) before using any: one round trip instead of K / NC.
-template <int T, int MT>
+template <int T, int MT, int NCW = Cfg<MT>::NCW>
 __device__ __forceinline__ void prep_x(const GemvArgs &a, float *xs, float *xsum, float *red) {
-    constexpr int NCW = Cfg<MT>::NCW, NC = NCW * 32;
+    constexpr int NC = NCW * 32;
     constexpr int XB = MT <= 2 ? 8 : 4;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = a.k;
@@ -204,11 +204,10 @@ __device__ __forceinline__ void flush_argmax(const GemvSeg &s, int m_used, unsig
     }
 }
 
-template <int T, int MT>
+template <int T, int MT, int NCW = Cfg<MT>::NCW>
 __device__ __forceinline__ void consume_unit(const GemvArgs &a, const GemvSeg &s, int r0, int r1, uint64_t *full,
                                              uint64_t *empty, const uint8_t *stg, const float *xs,
                                              const float2 *xsum, uint32_t cur = 0) {
-    constexpr int NCW = Cfg<MT>::NCW;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = a.k, U = K / 32, R = s.rows_per_stage, NS = a.ns;
     const int nst = (r1 - r0 + R - 1) / R;
@@ -254,12 +253,11 @@ __device__ __forceinline__ void consume_unit(const GemvArgs &a, const GemvSeg &s
     flush_argmax<MT>(s, a.m, best);
 }
 
-template <int T, int MT>
+template <int T, int MT, int NCW = Cfg<MT>::NCW>
 __device__ __forceinline__ void consume_wide(const GemvArgs &a, const GemvSeg &s, int r0, int r1, uint64_t *full,
                                              uint64_t *empty, const uint8_t *stg, const float *xw,
                                              const float *xs32, uint32_t cur = 0) {
     if constexpr (sb_supported<T>()) {
-        constexpr int NCW = Cfg<MT>::NCW;
         constexpr int SB = SpanBytes<T>::v;
         const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
         const int K = a.k, NSB = K / 256, R = s.rows_per_stage, NS = a.ns;

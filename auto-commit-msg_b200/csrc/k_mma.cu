@@ -10,9 +10,12 @@
 // K step, relative error ~1e-5.
 //
 // Layout.  Dequantization (exact, tensor.go:55-226) happens once per weight
-// tensor into two bf16 [n][K] arrays (the "split cache", 4 bytes per weight,
-// built on first use and kept in HBM); activations are split per call.  Both
-// are loaded by TMA into 128-byte-swizzled K-major tiles.
+// tensor into two bf16 arrays (the "split cache", 4 bytes per weight, built
+// on first use and kept in HBM); activations are split per call.  Both are
+// stored 64x64-blocked -- element (r, c) at ((r/64)*(K/64) + c/64)*4096 +
+// (r%64)*64 + c%64 -- so each TMA box is one contiguous 8 KB read (a
+// row-major [n][K] box gathers 64 pieces of 128 bytes from 64 DRAM pages),
+// and lands as a 128-byte-swizzled K-major tile.
 //
 // Kernel.  One CTA computes a tile of 128 weight rows x 64 tokens (for a
 // SwiGLU pair: 64 gate rows + the same 64 up rows) over the whole K:
@@ -177,20 +180,23 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_mma_gemm(const __grid_consta
             if (kt >= MST && !mbar_wait(&empty[s], ((kt / MST) & 1) ^ 1)) break;
             uint8_t *st = msm + s * STAGE_BYTES;
             mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-            const int kx = kt * MBK;
+            // 64x64 block (row block rb, K block kt) starts at box row (rb*KT + kt)*64
+            const int ya = ((row0 >> 6) * KT + kt) * 64, yb = ((tok0 >> 6) * KT + kt) * 64;
             if (S.pair) {
-                tma_load_2d(st, &S.ahi, kx, row0, &full[s]);
-                tma_load_2d(st + A_BYTES / 2, &S.ahi2, kx, row0, &full[s]);
-                tma_load_2d(st + A_BYTES, &S.alo, kx, row0, &full[s]);
-                tma_load_2d(st + A_BYTES + A_BYTES / 2, &S.alo2, kx, row0, &full[s]);
+                tma_load_2d(st, &S.ahi, 0, ya, &full[s]);
+                tma_load_2d(st + A_BYTES / 2, &S.ahi2, 0, ya, &full[s]);
+                tma_load_2d(st + A_BYTES, &S.alo, 0, ya, &full[s]);
+                tma_load_2d(st + A_BYTES + A_BYTES / 2, &S.alo2, 0, ya, &full[s]);
             } else {
-                tma_load_2d(st, &S.ahi, kx, row0, &full[s]);
-                tma_load_2d(st + A_BYTES / 2, &S.ahi, kx, row0 + 64, &full[s]);
-                tma_load_2d(st + A_BYTES, &S.alo, kx, row0, &full[s]);
-                tma_load_2d(st + A_BYTES + A_BYTES / 2, &S.alo, kx, row0 + 64, &full[s]);
+                // the second 64 rows: next row block (zero-filled past the cache)
+                const int ya2 = ya + KT * 64;
+                tma_load_2d(st, &S.ahi, 0, ya, &full[s]);
+                tma_load_2d(st + A_BYTES / 2, &S.ahi, 0, ya2, &full[s]);
+                tma_load_2d(st + A_BYTES, &S.alo, 0, ya, &full[s]);
+                tma_load_2d(st + A_BYTES + A_BYTES / 2, &S.alo, 0, ya2, &full[s]);
             }
-            tma_load_2d(st + 2 * A_BYTES, &A.bhi, kx, tok0, &full[s]);
-            tma_load_2d(st + 2 * A_BYTES + B_BYTES, &A.blo, kx, tok0, &full[s]);
+            tma_load_2d(st + 2 * A_BYTES, &A.bhi, 0, yb, &full[s]);
+            tma_load_2d(st + 2 * A_BYTES + B_BYTES, &A.blo, 0, yb, &full[s]);
             issued = kt + 1;
         }
         // no copy may still be landing when the CTA exits: wait (bounded)
@@ -288,14 +294,20 @@ __device__ __forceinline__ void split_bf16(float v, __nv_bfloat16 &hi, __nv_bflo
     lo = __float2bfloat16_rn(v - __bfloat162float(hi));
 }
 
-// x[m][ldx] fp32 -> hi, lo [m][k] bf16
+// Offset of element (r, c) in the 64x64-blocked layout of a [rows][k] matrix.
+__device__ __forceinline__ int64_t blk64(int64_t r, int c, int k) {
+    return (((r >> 6) * (k >> 6) + (c >> 6)) << 12) + ((r & 63) << 6) + (c & 63);
+}
+
+// x[m][ldx] fp32 -> hi, lo bf16, 64x64-blocked
 __global__ void k_split_act(const float *x, int ldx, int m, int k, __nv_bfloat16 *hi, __nv_bfloat16 *lo) {
     pdl_wait();
     if (threadIdx.x == 0) pdl_trigger();
     const int64_t total = (int64_t)m * k / 4;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t e = i * 4;
-        const int r = (int)(e / k), c = (int)(e - (int64_t)r * k);
+        const int64_t e0 = i * 4;
+        const int r = (int)(e0 / k), c = (int)(e0 - (int64_t)r * k);
+        const int64_t e = blk64(r, c, k);
         const float4 v = *reinterpret_cast<const float4 *>(x + (int64_t)r * ldx + c);
         __nv_bfloat16 h[4], l[4];
         split_bf16(v.x, h[0], l[0]);
@@ -307,7 +319,7 @@ __global__ void k_split_act(const float *x, int ldx, int m, int k, __nv_bfloat16
     }
 }
 
-// Exact dequantization of W [n][k] (ggml blocks) -> hi, lo [n][k] bf16.
+// Exact dequantization of W [n][k] (ggml blocks) -> hi, lo bf16, 64x64-blocked.
 template <int T>
 __global__ void k_split_weight(const uint8_t *w, int64_t n, int k, __nv_bfloat16 *hi, __nv_bfloat16 *lo) {
     const int64_t rb = row_bytes(T, k);
@@ -321,8 +333,9 @@ __global__ void k_split_weight(const uint8_t *w, int64_t n, int k, __nv_bfloat16
         __nv_bfloat16 h[32], l[32];
 #pragma unroll
         for (int j = 0; j < 32; j++) split_bf16(v[j], h[j], l[j]);
-        uint4 *ph = reinterpret_cast<uint4 *>(hi + r * k + run * 32);
-        uint4 *pl = reinterpret_cast<uint4 *>(lo + r * k + run * 32);
+        const int64_t e = blk64(r, run * 32, k);  // 32 consecutive elements stay contiguous
+        uint4 *ph = reinterpret_cast<uint4 *>(hi + e);
+        uint4 *pl = reinterpret_cast<uint4 *>(lo + e);
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             ph[j] = reinterpret_cast<const uint4 *>(h)[j];
@@ -364,14 +377,16 @@ bool mma_available() {
     return avail == 1;
 }
 
-// 2-D bf16 map over [rows][k] (row stride k elements), box {64, 64 rows},
-// 128-byte swizzle; rows beyond `rows` read as zero.
+// 2-D bf16 map over a 64x64-blocked [rows][k] matrix, seen as
+// (ceil(rows/64) * k/64 * 64) rows of 64 elements; box {64, 64 rows}, 128-byte
+// swizzle.  Boxes past the end read as zero.
 static_assert(sizeof(TensorMap) == sizeof(CUtensorMap), "tensor map storage");
 bool bf16_map(TensorMap *tmap, const void *base, int64_t rows, int64_t k) {
     CUtensorMap *map = reinterpret_cast<CUtensorMap *>(tmap);
     if (!encode_fn() || k % MBK || ((uintptr_t)base & 15)) return false;
-    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+    const int64_t rows2 = (rows + 63) / 64 * (k / 64) * 64;
+    cuuint64_t dims[2] = {(cuuint64_t)MBK, (cuuint64_t)rows2};
+    cuuint64_t strides[1] = {(cuuint64_t)MBK * 2};
     cuuint32_t box[2] = {MBK, 64};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,

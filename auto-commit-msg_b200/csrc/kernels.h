@@ -95,11 +95,13 @@ struct alignas(64) TensorMap {
     uint64_t w[16];  // CUtensorMap
 };
 bool mma_available();
-// 2-D bf16 tensor map over [rows][k] for the GEMM's 64x64 boxes.
+// Split operands are stored 64x64-blocked; buffers hold ceil(rows/64)*64 rows.
+// Tensor map over such a [rows][k] buffer for the GEMM's 64x64 boxes.
 bool bf16_map(TensorMap *map, const void *base, int64_t rows, int64_t k);
-// fp32 [m][ldx] -> bf16 hi, lo [m][k]
+inline int64_t rows64(int64_t rows) { return (rows + 63) / 64 * 64; }
+// fp32 [m][ldx] -> bf16 hi, lo (blocked)
 cudaError_t split_act_launch(const float *x, int ldx, int m, int k, void *hi, void *lo, cudaStream_t st);
-// exact dequant of W [n][k] -> bf16 hi, lo [n][k]
+// exact dequant of W [n][k] -> bf16 hi, lo (blocked)
 cudaError_t split_weight_launch(int type, const void *w, int64_t n, int k, void *hi, void *lo, cudaStream_t st);
 struct MmaGemmSeg {
     const TensorMap *map_hi, *map_lo;    // W split cache
