@@ -84,6 +84,8 @@ SIGNATURES = {
     "acm_engine_sync": (C.c_int, [P]),
     "acm_model_last_timing": (C.c_int, [P, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "acm_kernel_launches": (C.c_uint64, []),
+    "acm_model_bench_gemm": (C.c_int, [P, C.c_int32, C.c_int32, C.POINTER(C.c_double), C.POINTER(C.c_double),
+                                       C.POINTER(C.c_int32)]),
     "acm_serve": (C.c_int, [P, C.POINTER(CRequest), C.c_int32, C.c_int32, C.c_int32, C.POINTER(CStats)]),
     "acm_model_trace": (C.c_int, [P, C.c_int32]),
     "acm_model_trace_read": (C.c_int, [P, P, C.c_int64, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),

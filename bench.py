@@ -84,6 +84,26 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def tensor_peak():
+    """Dense bf16 TFLOP/s: the burst figure (kernels timed alone)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def bench_gemm(acm, m, ntok=PROMPT_LEN, reps=5):
+    """The prefill's tensor-core GEMM launches (q/k/v, o, gate/up, down x 28
+    layers at ntok tokens) timed with CUDA events: (s, useful flops, launches)
+    per pass, or None when the model has no tensor-core path."""
+    import ctypes as C
+    sec, fl, nl = C.c_double(), C.c_double(), C.c_int32()
+    if acm.lib().acm_model_bench_gemm(m.handle, ntok, reps, C.byref(sec), C.byref(fl), C.byref(nl)):
+        return None
+    return sec.value, fl.value, nl.value
+
+
 class Clocks:
     """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -213,6 +233,18 @@ def run_ours(args, rank, world, local):
             traffic = json.load(f).get("k_gemv_decode_pass_bytes")
     except Exception:
         pass
+    # prefill: the tensor-core GEMM launches of one 389-token prefill
+    prefill_roof = None
+    g = bench_gemm(acm, m)
+    if g:
+        gsec, gfl, gnl = g
+        tpk, tpk_kind = tensor_peak()
+        pipe = 3 * gfl / gsec / 1e12  # three bf16 products per K step on the tensor pipe
+        prefill_roof = {"bound": "tensor", "kernel": "k_mma_gemm (all GEMM launches of one 389-token prefill)",
+                        "achieved": round(pipe, 1), "peak": tpk, "unit": "TFLOP/s", "frac": round(pipe / tpk, 4),
+                        "peak_kind": tpk_kind, "useful_tflops": round(gfl / gsec / 1e12, 1),
+                        "note": "achieved counts the 3 bf16 products of the hi/lo split (3 x 2*M*N*K per GEMM)",
+                        "ms_per_pass": round(gsec * 1e3, 3), "launches_per_pass": gnl, "traffic": None}
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(1e3 * dev_max / args.steps, 3), "higher_is_better": True,
@@ -229,6 +261,7 @@ def run_ours(args, rank, world, local):
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "bytes_per_pass": int(nbytes), "launches_per_pass": nl, "traffic": traffic},
+        "prefill_roofline": prefill_roof,
         "gpu_launches": tot_launches,
         "clocks": ck,
     }
@@ -252,6 +285,53 @@ def bench_gemv(acm, m, reps=20):
     return sec.value, b.value, nl.value
 
 
+def run_profile(args):
+    """Short workloads for the profiler (no JSON line): `prefill` runs three
+    389-token prefills; `decode` one prefill + `--tokens` greedy decode tokens;
+    `trace` the same with the persistent decode kernel's per-phase timestamps
+    (acm_model_trace) and prints per-phase-kind spans of the last token."""
+    import ctypes as C
+
+    import numpy as np
+
+    acm = importlib.import_module("auto-commit-msg_b200")
+    lib = acm.lib()
+    path, prompt = model_path(0, 1)
+    eng = acm.Engine(0)
+    m = acm.Load(path, CTX, engine=eng)
+    if args.profile == "prefill":
+        for i in range(3):
+            m.Forward(prompt)
+            eng.sync()
+            print(f"prefill {i}: {1e3 * m.last_timing()[0]:.3f} ms", flush=True)
+            m.Reset()
+    else:
+        if args.profile == "trace":
+            rc = lib.acm_model_trace(m.handle, 1)
+            if rc:
+                print("trace unavailable:", lib.acm_last_error(m.handle).decode())
+                args.profile = "decode"
+        ids = m.Generate(prompt, acm.Sampler(0.0), args.tokens, stop_on_eos=False)
+        print(f"decode {args.tokens} tokens: {args.tokens / m.Stats.Decode:.1f} tok/s", flush=True)
+        if args.profile == "trace":
+            cap = 148 * 1024 * 2
+            buf = (C.c_uint64 * cap)()
+            nb, nph = C.c_int32(), C.c_int32()
+            if lib.acm_model_trace_read(m.handle, buf, cap, C.byref(nb), C.byref(nph)) == 0:
+                nb, nph = nb.value, nph.value
+                t = np.frombuffer(buf, dtype=np.uint64)[: nb * nph * 2].reshape(nb, nph, 2).astype(np.int64)
+                t -= t[:, 0, 0].min()
+                kinds = ["qkv", "attn", "o", "ffn", "down"]
+                print(f"persistent kernel: {nb} CTAs, {nph} phases, token {t[:, -1, 1].max() / 1e3:.1f} us")
+                for ki, kname in enumerate(kinds + ["lm_head"]):
+                    ps = [nph - 1] if kname == "lm_head" else list(range(ki, nph - 1, 5))
+                    span = [(t[:, p, 1].max() - t[:, p, 0].min()) / 1e3 for p in ps]
+                    work = [float(np.median(t[:, p, 1] - t[:, p, 0])) / 1e3 for p in ps]
+                    print(f"  {kname:8s} phases {len(ps):3d}  span {np.mean(span):7.2f} us  median CTA work {np.mean(work):6.2f} us")
+    m.close()
+    eng.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -259,7 +339,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--profile", choices=["prefill", "decode", "trace"],
+                    help="run a short workload for the profiler instead of the benchmark")
+    ap.add_argument("--tokens", type=int, default=8, help="decode tokens of --profile decode/trace")
     args = ap.parse_args()
+    if args.profile:
+        run_profile(args)
+        return
     rank, world, local = dist()
     try:
         if args.impl == "reference":

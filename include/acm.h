@@ -240,6 +240,15 @@ ACM_API uint64_t acm_kernel_launches(void);
 ACM_API int acm_model_trace(acm_model *m, int32_t enable);
 ACM_API int acm_model_trace_read(acm_model *m, uint64_t *out, int64_t cap, int32_t *nblocks, int32_t *nphases);
 
+/* Measurement helper, no reference counterpart: the tensor-core GEMM
+ * launches of one ntok-token prefill (q/k/v, o, gate/up, down of every layer:
+ * the matmul calls of model.go:346-348, :410, :418-419, :423) timed `reps`
+ * times with CUDA events on the model stream (scratch activations; the
+ * model's sequence state is untouched); seconds and useful flops
+ * (2*ntok*weights) per pass, launches per pass. */
+ACM_API int acm_model_bench_gemm(acm_model *m, int32_t ntok, int32_t reps, double *sec_per_pass,
+                                 double *flops_per_pass, int32_t *launches_per_pass);
+
 /* Measurement helper, no reference counterpart: replay the fused
  * dequant-GEMV launches of one batch-1 decode token on this model's weights
  * (q/k/v, o, gate/up, down of every layer, then lm_head -- the matvec calls of
