@@ -146,9 +146,16 @@ struct acm_model {
     // tensor-core GEMM: activations split into bf16 hi/lo [T][kmax] and their
     // tensor maps for K = n_embd, q_dim, n_ff
     void *xs_hi = nullptr, *xs_lo = nullptr;
+    float *mma_ws = nullptr;  // split-K partial sums [4][T][max(n_embd, q_dim)]
+    size_t mma_ws_floats = 0;
     TensorMap xmap_hi[3], xmap_lo[3];
     int xmap_k[3] = {0, 0, 0};
     int mma_state = 0;  // 0 untried, 1 usable, -1 unavailable
+    // prefill attention on the tensor cores: split operands, scores, weights
+    void *aq_hi = nullptr, *aq_lo = nullptr, *ak_hi = nullptr, *ak_lo = nullptr, *av_hi = nullptr, *av_lo = nullptr,
+         *ap_hi = nullptr, *ap_lo = nullptr;
+    float *as = nullptr;
+    int attn_mma_state = 0;
 
     // per-token metadata and sampler state (device + pinned staging)
     int32_t *d_tok = nullptr, *d_seq = nullptr, *d_pos = nullptr, *d_out = nullptr, *d_topk = nullptr;
@@ -295,6 +302,11 @@ bool mma_ready(acm_model *m) {
         cudaGetLastError();
         return false;
     }
+    m->mma_ws_floats = 4 * T * (size_t)std::max(c.n_embd, qd);
+    if (dalloc(m, &m->mma_ws, m->mma_ws_floats) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
     for (int i = 0; i < 3; i++) {
         if (ks[i] % 64) return false;
         m->xmap_k[i] = ks[i];
@@ -315,6 +327,93 @@ int mma_split_x(acm_model *m, const float *x, int ldx, int ntok, int k, const Te
     CK_M(split_act_launch(x, ldx, ntok, k, m->xs_hi, m->xs_lo, m->e->stream));
     *hi = &m->xmap_hi[i];
     *lo = &m->xmap_lo[i];
+    return ACM_OK;
+}
+
+// Buffers of the tensor-core prefill attention, for chunks of up to TMAX
+// tokens and contexts of up to max_ctx positions (limited to 8192: the score
+// matrix is [kv heads][G * TMAX][max_ctx] fp32).
+bool attn_mma_ready(acm_model *m) {
+    if (m->attn_mma_state) return m->attn_mma_state > 0;
+    m->attn_mma_state = -1;
+    const acm_config &c = m->c;
+    const char *env = getenv("ACM_ATTN_MMA");
+    if ((env && env[0] == '0') || !mma_ready(m)) return false;
+    const int hd = c.head_dim, nkv = c.n_head_kv, G = c.n_head / c.n_head_kv;
+    if (hd % 64 || hd > 128 || c.max_ctx > 8192 || PAGE % 64) return false;
+    const size_t rq = (size_t)rows64((int64_t)G * TMAX), lp = (size_t)rows64(c.max_ctx);
+    const size_t nq = nkv * rq * hd, nk = nkv * lp * hd, np = nkv * rq * lp;
+    auto al16 = [&](void **p, size_t n) {
+        return dalloc(m, reinterpret_cast<uint16_t **>(p), n) == cudaSuccess;
+    };
+    if (!al16(&m->aq_hi, nq) || !al16(&m->aq_lo, nq) || !al16(&m->ak_hi, nk) || !al16(&m->ak_lo, nk) ||
+        !al16(&m->av_hi, nk) || !al16(&m->av_lo, nk) || !al16(&m->ap_hi, np) || !al16(&m->ap_lo, np) ||
+        dalloc(m, &m->as, (size_t)nkv * G * TMAX * lp) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    m->attn_mma_state = 1;
+    return true;
+}
+
+// Prefill attention of one layer on the tensor cores: the chunk's tokens are
+// consecutive positions pos0 .. pos0 + ntok - 1 of sequence `seq` (keys and
+// values already appended).  S = Q.K^T and O = P.V as batched split-bf16
+// GEMMs over the kv heads, the reference's softmax between them.
+int attention_prefill_mma(acm_model *m, int layer, int seq, int pos0, int ntok) {
+    const acm_config &c = m->c;
+    cudaStream_t st = m->e->stream;
+    const int hd = c.head_dim, nkv = c.n_head_kv, G = c.n_head / c.n_head_kv, nh = c.n_head;
+    const int L = pos0 + ntok, Lp = (int)rows64(L), rows = G * ntok;
+    const int64_t rq = rows64(rows);
+    AttnMmaOps o{};
+    o.q = m->q;
+    o.kc = m->kpool;
+    o.vc = m->vpool;
+    o.page_row = m->d_page_table + (int64_t)seq * m->max_pages;
+    o.layer_off = (int64_t)layer * m->layer_stride;
+    o.page_size = PAGE;
+    o.kvd = nkv * hd;
+    o.ntok = ntok;
+    o.L = L;
+    o.Lp = Lp;
+    o.G = G;
+    o.nh = nh;
+    o.hd = hd;
+    o.nkv = nkv;
+    o.pos0 = pos0;
+    o.rq = rq;
+    o.scale = 1.0f / (float)sqrt((double)hd);
+    o.qh = m->aq_hi; o.ql = m->aq_lo; o.kh = m->ak_hi; o.kl = m->ak_lo;
+    o.vh = m->av_hi; o.vl = m->av_lo; o.ph = m->ap_hi; o.pl = m->ap_lo;
+    o.S = m->as;
+    CK_M(attn_split_launch(o, st));
+    TensorMap kh, kl, qh, ql, vh, vl, ph, pl;
+    if (!bf16_map(&kh, m->ak_hi, (int64_t)nkv * Lp, hd) || !bf16_map(&kl, m->ak_lo, (int64_t)nkv * Lp, hd) ||
+        !bf16_map(&qh, m->aq_hi, nkv * rq, hd) || !bf16_map(&ql, m->aq_lo, nkv * rq, hd) ||
+        !bf16_map(&vh, m->av_hi, (int64_t)nkv * hd, Lp) || !bf16_map(&vl, m->av_lo, (int64_t)nkv * hd, Lp) ||
+        !bf16_map(&ph, m->ap_hi, nkv * rq, Lp) || !bf16_map(&pl, m->ap_lo, nkv * rq, Lp))
+        return set_err(m, ACM_ERR_CUDA, "tensor map encoding failed");
+    // S[g][r][p] = Qs[g][r] . Ks[g][p]
+    MmaGemmSeg sq{&kh, &kl, nullptr, nullptr, L, EPI_STORE, m->as, Lp, nullptr, nullptr};
+    MmaBatch bq;
+    bq.n = nkv;
+    bq.a_stride = (Lp / 64) * (hd / 64) * 64;
+    bq.b_stride = (int)(rq / 64) * (hd / 64) * 64;
+    bq.rbatch = rows;
+    CK_M(mma_gemm_batched_launch(&sq, 1, &qh, &ql, rows, hd, bq, st));
+    CK_M(attn_softmax_launch(o, st));
+    // att[t][(g*G + h)*hd + d] = P[g][h*ntok + t] . Vt[g][d]
+    MmaGemmSeg sv{&vh, &vl, nullptr, nullptr, hd, EPI_STORE, m->att, hd, nullptr, nullptr};
+    MmaBatch bv;
+    bv.n = nkv;
+    bv.a_stride = (hd / 64) * (Lp / 64) * 64;
+    bv.b_stride = (int)(rq / 64) * (Lp / 64) * 64;
+    bv.rmod = ntok;
+    bv.rmul = nh;
+    bv.rdiv = 1;
+    bv.rbatch = G;
+    CK_M(mma_gemm_batched_launch(&sv, 1, &ph, &pl, rows, Lp, bv, st));
     return ACM_OK;
 }
 
@@ -374,8 +473,12 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
         } else {
             CK_M(rope_append_launch(rd, kv, l, tm, ntok, st));
             // a prefill chunk: consecutive positions of one sequence
-            AttnDesc ad{m->q, m->att, c.n_head, c.n_head_kv, hd, scale, m->part, nsplit, nullptr};
-            CK_M(attention_prefill_launch(ad, kv, l, tm, ntok, st));
+            if (ntok > 8 && attn_mma_ready(m)) {
+                if (int rc = attention_prefill_mma(m, l, m->h_seq.p[0], m->h_pos.p[0], ntok)) return rc;
+            } else {
+                AttnDesc ad{m->q, m->att, c.n_head, c.n_head_kv, hd, scale, m->part, nsplit, nullptr};
+                CK_M(attention_prefill_launch(ad, kv, l, tm, ntok, st));
+            }
         }
         // x += Wo att
         if (gemv_supported(L.o->type, qd, ntok)) {
@@ -385,7 +488,7 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
             const TensorMap *xh, *xl;
             if (int rc = mma_split_x(m, m->att, qd, ntok, qd, &xh, &xl)) return rc;
             MmaGemmSeg so{&L.o->mhi, &L.o->mlo, nullptr, nullptr, E, EPI_ADD, m->x, E, nullptr, nullptr};
-            CK_M(mma_gemm_launch(&so, 1, xh, xl, ntok, qd, st));
+            CK_M(mma_gemm_launch(&so, 1, xh, xl, ntok, qd, st, m->mma_ws, m->mma_ws_floats));
         } else {
             CK_M(gemm_launch({L.o->d, nullptr, (int)L.o->type, E, qd, ntok, m->att, qd, m->x, E, EPI_ADD, nullptr, nullptr}, st));
         }
@@ -426,7 +529,7 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
             const TensorMap *xh, *xl;
             if (int rc = mma_split_x(m, m->hb, F, ntok, F, &xh, &xl)) return rc;
             MmaGemmSeg sd{&L.down->mhi, &L.down->mlo, nullptr, nullptr, E, EPI_ADD, m->x, E, nullptr, nullptr};
-            CK_M(mma_gemm_launch(&sd, 1, xh, xl, ntok, F, st));
+            CK_M(mma_gemm_launch(&sd, 1, xh, xl, ntok, F, st, m->mma_ws, m->mma_ws_floats));
         } else {
             CK_M(gemm_launch({L.down->d, nullptr, (int)L.down->type, E, F, ntok, m->hb, F, m->x, E, EPI_ADD, nullptr, nullptr}, st));
         }
@@ -1511,11 +1614,11 @@ ACM_API int acm_model_bench_gemm(acm_model *m, int32_t ntok, int32_t reps, doubl
                                 {&L.v->mhi, &L.v->mlo, nullptr, nullptr, kvd, EPI_STORE, m->v, kvd, L.v_b, nullptr}};
             CK_M(mma_gemm_launch(sg, 3, xe_h, xe_l, ntok, E, st));
             MmaGemmSeg so{&L.o->mhi, &L.o->mlo, nullptr, nullptr, E, EPI_STORE, m->h, E, nullptr, nullptr};
-            CK_M(mma_gemm_launch(&so, 1, xq_h, xq_l, ntok, qd, st));
+            CK_M(mma_gemm_launch(&so, 1, xq_h, xq_l, ntok, qd, st, m->mma_ws, m->mma_ws_floats));
             MmaGemmSeg sf{&L.gate->mhi, &L.gate->mlo, &L.up->mhi, &L.up->mlo, F, EPI_SWIGLU, m->hb2, F, nullptr, nullptr};
             CK_M(mma_gemm_launch(&sf, 1, xe_h, xe_l, ntok, E, st));
             MmaGemmSeg sd{&L.down->mhi, &L.down->mlo, nullptr, nullptr, E, EPI_STORE, m->h, E, nullptr, nullptr};
-            CK_M(mma_gemm_launch(&sd, 1, xf_h, xf_l, ntok, F, st));
+            CK_M(mma_gemm_launch(&sd, 1, xf_h, xf_l, ntok, F, st, m->mma_ws, m->mma_ws_floats));
             flops += 2.0 * ntok * ((double)(qd + 2 * kvd) * E + (double)E * qd + 2.0 * F * E + (double)E * F);
             nl += 4;
         }
@@ -1684,9 +1787,11 @@ ACM_API int acm_matmul_dev(acm_engine *e, uint32_t ggml_type, const void *d_w, i
     } else if (k % 64 == 0 && mma_available()) {
         // tensor-core path: split W and x to bf16 hi/lo in the second scratch
         const size_t wbs = al256((size_t)rows64(n) * k * 2), xbs = al256((size_t)rows64(m) * k * 2);
+        const size_t wsf = 4 * (size_t)m * n;  // split-K partial sums
         uint8_t *s2 = nullptr;
-        if (int rc = scratch2(e, 2 * wbs + 2 * xbs, &s2)) return rc;
+        if (int rc = scratch2(e, 2 * wbs + 2 * xbs + wsf * 4, &s2)) return rc;
         uint8_t *whi = s2, *wlo = s2 + wbs, *xhi = s2 + 2 * wbs, *xlo = xhi + xbs;
+        float *ws = reinterpret_cast<float *>(xlo + xbs);
         CK_E(split_weight_launch((int)ggml_type, d_w, n, (int)k, whi, wlo, e->stream));
         CK_E(split_act_launch(d_x, (int)k, m, (int)k, xhi, xlo, e->stream));
         TensorMap mwh, mwl, mxh, mxl;
@@ -1694,7 +1799,7 @@ ACM_API int acm_matmul_dev(acm_engine *e, uint32_t ggml_type, const void *d_w, i
             !bf16_map(&mxl, xlo, m, k))
             return set_eerr(e, ACM_ERR_CUDA, "tensor map encoding failed");
         MmaGemmSeg sg{&mwh, &mwl, nullptr, nullptr, n, EPI_STORE, d_y, (int)n, nullptr, nullptr};
-        CK_E(mma_gemm_launch(&sg, 1, &mxh, &mxl, m, (int)k, e->stream));
+        CK_E(mma_gemm_launch(&sg, 1, &mxh, &mxl, m, (int)k, e->stream, ws, wsf));
     } else {
         CK_E(gemm_launch({d_w, nullptr, (int)ggml_type, n, k, m, d_x, (int)k, d_y, (int)n, EPI_STORE, nullptr, nullptr},
                          e->stream));

@@ -31,6 +31,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
+#include <float.h>
 #include <stdio.h>
 #include <string.h>
 
@@ -129,7 +130,20 @@ struct MmaArgs {
     CUtensorMap bhi, blo;  // activations split, box {64, 64 rows}
     int m, k;
     int ttiles;            // token tiles
+    // batched form (blockIdx.y = batch, one segment): operand offsets in box
+    // rows, and the output row of token `tok` of batch b:
+    // (rmod ? (tok % rmod) * rmul + (tok / rmod) * rdiv : tok) + b * rbatch
+    int a_bstride, b_bstride, rmod, rmul, rdiv, rbatch;
+    // split-K (blockIdx.z = K slice): partial sums to ws[slice][tok][n]
+    int ksplit;
+    float *ws;
 };
+
+__device__ __forceinline__ int64_t out_row(const MmaArgs &A, const MmaSeg &S, int tok, int batch) {
+    if (S.yrow) return S.yrow[tok];
+    const int r = A.rmod ? (tok % A.rmod) * A.rmul + (tok / A.rmod) * A.rdiv : tok;
+    return (int64_t)r + (int64_t)batch * A.rbatch;
+}
 
 __global__ void __launch_bounds__(MMA_THREADS, 1) k_mma_gemm(const __grid_constant__ MmaArgs A) {
     extern __shared__ uint8_t msm_raw[];
@@ -149,7 +163,11 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_mma_gemm(const __grid_consta
     const int rt = local / A.ttiles, tt = local - rt * A.ttiles;
     const int rows_per_tile = S.pair ? MBM / 2 : MBM;
     const int row0 = rt * rows_per_tile, tok0 = tt * MBN;
-    const int KT = A.k / MBK;
+    const int batch = blockIdx.y;
+    // this CTA's K blocks: all of them, or its slice under split-K
+    const int KTA = A.k / MBK;  // K blocks of the operands (their layout)
+    const int kb0 = (int)((int64_t)KTA * blockIdx.z / A.ksplit), kb1 = (int)((int64_t)KTA * (blockIdx.z + 1) / A.ksplit);
+    const int KT = kb1 - kb0;
 
     if (tid == 0) {
         for (int i = 0; i < MST; i++) {
@@ -181,7 +199,8 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_mma_gemm(const __grid_consta
             uint8_t *st = msm + s * STAGE_BYTES;
             mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
             // 64x64 block (row block rb, K block kt) starts at box row (rb*KT + kt)*64
-            const int ya = ((row0 >> 6) * KT + kt) * 64, yb = ((tok0 >> 6) * KT + kt) * 64;
+            const int ya = ((row0 >> 6) * KTA + kb0 + kt) * 64 + batch * A.a_bstride;
+            const int yb = ((tok0 >> 6) * KTA + kb0 + kt) * 64 + batch * A.b_bstride;
             if (S.pair) {
                 tma_load_2d(st, &S.ahi, 0, ya, &full[s]);
                 tma_load_2d(st + A_BYTES / 2, &S.ahi2, 0, ya, &full[s]);
@@ -189,7 +208,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_mma_gemm(const __grid_consta
                 tma_load_2d(st + A_BYTES + A_BYTES / 2, &S.alo2, 0, ya, &full[s]);
             } else {
                 // the second 64 rows: next row block (zero-filled past the cache)
-                const int ya2 = ya + KT * 64;
+                const int ya2 = ya + KTA * 64;
                 tma_load_2d(st, &S.ahi, 0, ya, &full[s]);
                 tma_load_2d(st + A_BYTES / 2, &S.ahi, 0, ya2, &full[s]);
                 tma_load_2d(st + A_BYTES, &S.alo, 0, ya, &full[s]);
@@ -250,12 +269,21 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_mma_gemm(const __grid_consta
                             if (n < S.n && tok < A.m) {
                                 const float g = v[j], u = xch[lrow * (MBN + 1) + c0 + j];
                                 const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, fast_exp(-g)));
-                                float *yp = S.y + (int64_t)(S.yrow ? S.yrow[tok] : tok) * S.ldy + n;
+                                float *yp = S.y + out_row(A, S, tok, batch) * S.ldy + n;
                                 *yp = __fmul_rn(__fmul_rn(g, sg), u);
                             }
                         }
                     }
                     named_sync(1, 128);
+                } else if (A.ksplit > 1) {
+                    // partial sums of this K slice (bias and epilogue in k_split_reduce)
+                    const int n = row0 + lrow;
+                    if (n < S.n)
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            const int tok = tok0 + c0 + j;
+                            if (tok < A.m) A.ws[((int64_t)blockIdx.z * A.m + tok) * S.n + n] = v[j];
+                        }
                 } else {
                     const int n = row0 + lrow;
                     if (n < S.n) {
@@ -264,7 +292,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_mma_gemm(const __grid_consta
                         for (int j = 0; j < 16; j++) {
                             const int tok = tok0 + c0 + j;
                             if (tok < A.m) {
-                                float *yp = S.y + (int64_t)(S.yrow ? S.yrow[tok] : tok) * S.ldy + n;
+                                float *yp = S.y + out_row(A, S, tok, batch) * S.ldy + n;
                                 const float val = S.bias ? v[j] + b : v[j];
                                 if (S.epi == EPI_ADD) *yp = *yp + val;
                                 else *yp = val;
@@ -283,6 +311,23 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_mma_gemm(const __grid_consta
         mbar_wait(accf, 0);
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
+// Split-K epilogue: y[tok][n] (epi)= bias[n] + sum over slices, in slice
+// order (deterministic).
+__global__ void k_split_reduce(const float *ws, int ks, int m, int n, float *y, int ldy, int epi, const float *bias,
+                               const int32_t *yrow) {
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
+    const int64_t total = (int64_t)m * n;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int tok = (int)(i / n), c = (int)(i - (int64_t)tok * n);
+        float v = ws[i];
+        for (int s = 1; s < ks; s++) v += ws[(int64_t)s * total + i];
+        if (bias) v += bias[c];
+        float *yp = y + (int64_t)(yrow ? yrow[tok] : tok) * ldy + c;
+        *yp = epi == EPI_ADD ? *yp + v : v;
     }
 }
 
@@ -341,6 +386,109 @@ __global__ void k_split_weight(const uint8_t *w, int64_t n, int k, __nv_bfloat16
             ph[j] = reinterpret_cast<const uint4 *>(h)[j];
             pl[j] = reinterpret_cast<const uint4 *>(l)[j];
         }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Prefill attention operands (model.go:384-408 for a chunk of consecutive
+// positions of one sequence), for S = Q.K^T and O = P.V on the tensor cores.
+// Per kv head g (the batch index):
+//   Qs [G*ntok][HD]  row h*ntok + t = query head g*G + h of token t
+//   Ks [Lp][HD]      row p = cached key of position p (zero for p >= L)
+//   Vt [HD][Lp]      Vt[d][p] = V[p][d] (zero for p >= L)
+//   P  [G*ntok][Lp]  softmax weights
+// all split to bf16 hi/lo and 64x64-blocked; Lp = L rounded up to 64.
+// ---------------------------------------------------------------------------
+struct AttnSplitArgs {
+    const float *q;             // [ntok][nh*HD] (normed + roped)
+    const float *kc, *vc;       // cache pools
+    const int32_t *page_row;    // page table row of the sequence
+    int64_t layer_off;          // floats
+    int page_size, kvd;
+    int ntok, L, Lp, G, nh, hd;
+    int64_t rq;                 // rows64(G*ntok)
+    __nv_bfloat16 *qh, *ql, *kh, *kl, *vh, *vl;
+};
+
+// blockIdx.x < Lp/64: key block (K and V^T of 64 positions); beyond: query
+// row block of Qs.  blockIdx.y = kv head.  256 threads; HD <= 128.
+__global__ void __launch_bounds__(256) k_attn_split(const AttnSplitArgs a) {
+    extern __shared__ float asm_[];  // [64][HD + 1] for the V transpose
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
+    const int g = blockIdx.y, hd = a.hd, tid = threadIdx.x;
+    const int nkb = a.Lp / 64;
+    if ((int)blockIdx.x < nkb) {
+        const int p0 = blockIdx.x * 64;
+        // the 64 positions lie in one page (page size a multiple of 64)
+        const int64_t rowbase = a.layer_off + ((int64_t)a.page_row[p0 / a.page_size] * a.page_size +
+                                               (p0 % a.page_size)) * a.kvd + (int64_t)g * hd;
+        const int64_t kbase = (int64_t)g * a.Lp * hd, vbase = kbase;
+        for (int i = tid; i < 64 * hd; i += 256) {
+            const int pr = i / hd, d = i - pr * hd, p = p0 + pr;
+            const bool ok = p < a.L;
+            const float kv = ok ? a.kc[rowbase + (int64_t)pr * a.kvd + d] : 0.f;
+            const float vv = ok ? a.vc[rowbase + (int64_t)pr * a.kvd + d] : 0.f;
+            __nv_bfloat16 h, l;
+            split_bf16(kv, h, l);
+            const int64_t ek = kbase + blk64(p, d, hd);
+            a.kh[ek] = h;
+            a.kl[ek] = l;
+            asm_[pr * (hd + 1) + d] = vv;
+        }
+        __syncthreads();
+        for (int i = tid; i < 64 * hd; i += 256) {
+            const int d = i / 64, pr = i - d * 64;
+            __nv_bfloat16 h, l;
+            split_bf16(asm_[pr * (hd + 1) + d], h, l);
+            const int64_t ev = vbase + blk64(d, p0 + pr, a.Lp);
+            a.vh[ev] = h;
+            a.vl[ev] = l;
+        }
+    } else {
+        const int r0 = (blockIdx.x - nkb) * 64;
+        const int rows = a.G * a.ntok;
+        const int64_t qbase = (int64_t)g * a.rq * hd;
+        for (int i = tid; i < 64 * hd; i += 256) {
+            const int rr = i / hd, d = i - rr * hd, r = r0 + rr;
+            if (r >= rows) continue;
+            const int h = r / a.ntok, t = r - h * a.ntok;
+            __nv_bfloat16 hi, lo;
+            split_bf16(a.q[(int64_t)t * a.nh * hd + (int64_t)(g * a.G + h) * hd + d], hi, lo);
+            const int64_t e = qbase + blk64(r, d, hd);
+            a.qh[e] = hi;
+            a.ql[e] = lo;
+        }
+    }
+}
+
+// Softmax of one score row per warp (model.go:297-313 on the scaled scores
+// of positions <= the token's own): s = dot * scale, m = max s, e =
+// fastExp(s - m), p = e / sum e; written as split bf16 into P (zero past the
+// token's position).  grid (ceil(G*ntok / 8), nkv), 256 threads.
+__global__ void __launch_bounds__(256) k_attn_softmax(const float *S, int ntok, int G, int Lp, int pos0, float scale,
+                                                      int64_t rq, __nv_bfloat16 *ph, __nv_bfloat16 *pl) {
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
+    const int g = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rows = G * ntok, r = blockIdx.x * 8 + warp;
+    if (r >= rows) return;
+    const int t = r % ntok, n = pos0 + t + 1;  // keys 0 .. pos0 + t
+    const float *row = S + ((int64_t)g * rows + r) * Lp;
+    float mx = -FLT_MAX;
+    for (int p = lane; p < n; p += 32) mx = fmaxf(mx, __fmul_rn(__ldcg(row + p), scale));
+    mx = warp_max(mx);
+    float sum = 0.f;
+    for (int p = lane; p < n; p += 32) sum += fast_exp(__fsub_rn(__fmul_rn(__ldcg(row + p), scale), mx));
+    sum = warp_sum(sum);
+    const int64_t base = (int64_t)g * rq * Lp;
+    for (int p = lane; p < Lp; p += 32) {
+        const float e = p < n ? fast_exp(__fsub_rn(__fmul_rn(__ldcg(row + p), scale), mx)) : 0.f;
+        __nv_bfloat16 h, l;
+        split_bf16(p < n ? __fdiv_rn(e, sum) : 0.f, h, l);
+        const int64_t o = base + blk64(r, p, Lp);
+        ph[o] = h;
+        pl[o] = l;
     }
 }
 
@@ -427,11 +575,45 @@ cudaError_t split_weight_launch(int type, const void *w, int64_t n, int k, void 
     return launched(1);
 }
 
+cudaError_t attn_split_launch(const AttnMmaOps &o, cudaStream_t st) {
+    if (o.hd > 128 || o.hd % 64 || o.page_size % 64 || o.Lp % 64) return cudaErrorInvalidValue;
+    AttnSplitArgs a{o.q,  o.kc, o.vc, o.page_row, o.layer_off, o.page_size, o.kvd, o.ntok, o.L,  o.Lp, o.G,
+                    o.nh, o.hd, o.rq, static_cast<__nv_bfloat16 *>(o.qh), static_cast<__nv_bfloat16 *>(o.ql),
+                    static_cast<__nv_bfloat16 *>(o.kh), static_cast<__nv_bfloat16 *>(o.kl),
+                    static_cast<__nv_bfloat16 *>(o.vh), static_cast<__nv_bfloat16 *>(o.vl)};
+    const size_t smem = (size_t)64 * (o.hd + 1) * sizeof(float);
+    const int nqb = (int)((o.G * (int64_t)o.ntok + 63) / 64);
+    cudaError_t e = launch_pdl(k_attn_split, dim3(o.Lp / 64 + nqb, o.nkv), dim3(256), smem, st, a);
+    if (e != cudaSuccess) return e;
+    return launched(1);
+}
+
+cudaError_t attn_softmax_launch(const AttnMmaOps &o, cudaStream_t st) {
+    const int rows = o.G * o.ntok;
+    cudaError_t e = launch_pdl(k_attn_softmax, dim3((rows + 7) / 8, o.nkv), dim3(256), 0, st, o.S, o.ntok, o.G, o.Lp,
+                               o.pos0, o.scale, o.rq, static_cast<__nv_bfloat16 *>(o.ph),
+                               static_cast<__nv_bfloat16 *>(o.pl));
+    if (e != cudaSuccess) return e;
+    return launched(1);
+}
+
 cudaError_t mma_gemm_launch(const MmaGemmSeg *segs, int nseg, const TensorMap *x_hi, const TensorMap *x_lo, int m,
-                            int k, cudaStream_t st) {
-    if (nseg < 1 || nseg > MMA_MAX_SEG || m <= 0 || k % MBK) return cudaErrorInvalidValue;
+                            int k, cudaStream_t st, float *ws, size_t ws_floats) {
+    return mma_gemm_batched_launch(segs, nseg, x_hi, x_lo, m, k, MmaBatch{}, st, ws, ws_floats);
+}
+
+cudaError_t mma_gemm_batched_launch(const MmaGemmSeg *segs, int nseg, const TensorMap *x_hi, const TensorMap *x_lo,
+                                    int m, int k, const MmaBatch &bt, cudaStream_t st, float *ws, size_t ws_floats) {
+    if (nseg < 1 || nseg > MMA_MAX_SEG || m <= 0 || k % MBK || bt.n < 1 || (bt.n > 1 && nseg != 1))
+        return cudaErrorInvalidValue;
     MmaArgs a;
     memset(&a, 0, sizeof(a));
+    a.a_bstride = bt.a_stride;
+    a.b_bstride = bt.b_stride;
+    a.rmod = bt.rmod;
+    a.rmul = bt.rmul;
+    a.rdiv = bt.rdiv;
+    a.rbatch = bt.rbatch;
     a.nseg = nseg;
     a.m = m;
     a.k = k;
@@ -467,8 +649,26 @@ cudaError_t mma_gemm_launch(const MmaGemmSeg *segs, int nseg, const TensorMap *x
         if (e != cudaSuccess) return e;
         attr[dev & 63] = true;
     }
-    cudaError_t e = launch_pdl(k_mma_gemm, dim3(tiles), dim3(MMA_THREADS), MMA_SMEM, st, a);
+    // split-K when the tiles leave most SMs idle and K is long: one
+    // segment, no SwiGLU pair, not batched, a workspace for the partials
+    a.ksplit = 1;
+    const int KTA = k / MBK;
+    if (nseg == 1 && bt.n == 1 && !a.seg[0].pair && ws && tiles * 2 <= 148 && KTA >= 16) {
+        int ks = std::min(KTA / 8, 148 / tiles);
+        while (ks > 1 && (size_t)ks * m * segs[0].n > ws_floats) ks--;
+        a.ksplit = std::max(1, ks);
+        a.ws = ws;
+    }
+    cudaError_t e = launch_pdl(k_mma_gemm, dim3(tiles, bt.n, a.ksplit), dim3(MMA_THREADS), MMA_SMEM, st, a);
     if (e != cudaSuccess) return e;
+    if (a.ksplit > 1) {
+        const int64_t total = (int64_t)m * segs[0].n;
+        const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
+        e = launch_pdl(k_split_reduce, dim3(grid), dim3(256), 0, st, (const float *)ws, a.ksplit, m, (int)segs[0].n,
+                       segs[0].y, segs[0].ldy, segs[0].epi, segs[0].bias, segs[0].yrow);
+        if (e != cudaSuccess) return e;
+        return launched(2);
+    }
     return launched(1);
 }
 

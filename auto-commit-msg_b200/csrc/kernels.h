@@ -113,8 +113,38 @@ struct MmaGemmSeg {
     const float *bias;
     const int32_t *yrow;
 };
+// ws (optional, ws_floats floats): workspace for split-K partial sums, used
+// when the output tiles would leave most SMs idle.
 cudaError_t mma_gemm_launch(const MmaGemmSeg *segs, int nseg, const TensorMap *x_hi, const TensorMap *x_lo, int m,
-                            int k, cudaStream_t st);
+                            int k, cudaStream_t st, float *ws = nullptr, size_t ws_floats = 0);
+// Batched form: n independent GEMMs of the same shape (one segment) whose
+// operands follow each other in the split buffers (a_stride / b_stride: the
+// per-batch offset in 64-element box rows, i.e. rows64(rows) * k / 64); the
+// output row of token tok of batch b is (rmod ? (tok % rmod) * rmul +
+// (tok / rmod) * rdiv : tok) + b * rbatch.
+struct MmaBatch {
+    int n = 1;
+    int a_stride = 0, b_stride = 0;
+    int rmod = 0, rmul = 0, rdiv = 0, rbatch = 0;
+};
+cudaError_t mma_gemm_batched_launch(const MmaGemmSeg *segs, int nseg, const TensorMap *x_hi, const TensorMap *x_lo,
+                                    int m, int k, const MmaBatch &bt, cudaStream_t st, float *ws = nullptr,
+                                    size_t ws_floats = 0);
+
+// Prefill attention on the tensor cores: operand preparation (k_attn_split)
+// and the softmax between S = Q.K^T and O = P.V (k_attn_softmax).
+struct AttnMmaOps {
+    const float *q, *kc, *vc;
+    const int32_t *page_row;
+    int64_t layer_off;
+    int page_size, kvd, ntok, L, Lp, G, nh, hd, nkv, pos0;
+    int64_t rq;            // rows64(G * ntok)
+    float scale;
+    void *qh, *ql, *kh, *kl, *vh, *vl, *ph, *pl;
+    const float *S;        // [nkv][G*ntok][Lp] scores
+};
+cudaError_t attn_split_launch(const AttnMmaOps &o, cudaStream_t st);
+cudaError_t attn_softmax_launch(const AttnMmaOps &o, cudaStream_t st);
 
 // Dequantize rows (exact): rows either consecutive (row_ids == nullptr) or
 // gathered by id (embedding lookup, model.go:338-340).
