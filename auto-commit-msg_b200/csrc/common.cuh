@@ -58,6 +58,12 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// Pull [p, p + bytes) into L2 (p 16-byte aligned, bytes a multiple of 16);
+// completes on its own, nothing waits for it.
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Programmatic dependent launch: wait for the preceding kernel in the stream
 // (all its memory operations visible), and allow the next one to start its
 // CTAs early.  Both are no-ops when the launch did not opt in.

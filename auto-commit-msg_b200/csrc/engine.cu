@@ -450,7 +450,11 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
             GemvSegDesc sg[3] = {{L.q->d, nullptr, (int)L.q->type, qd, EPI_STORE, m->q, qd, L.q_b, nullptr},
                                  {L.k->d, nullptr, (int)L.k->type, kvd, EPI_STORE, m->k, kvd, L.k_b, nullptr},
                                  {L.v->d, nullptr, (int)L.v->type, kvd, EPI_STORE, m->v, kvd, L.v_b, nullptr}};
-            CK_M(gemv_launch(sg, 3, m->x, E, E, ntok, L.attn_nw, eps, S, st));
+            // each matvec pulls the next one's weights into L2 (decode: weights
+            // > L2 per token, so without this the next kernel's first stages
+            // pay a DRAM round trip on the critical path)
+            const L2Range pf_o[1] = {{L.o->d, (int64_t)L.o->nbytes}};
+            CK_M(gemv_launch(sg, 3, m->x, E, E, ntok, L.attn_nw, eps, S, st, pf_o, 1));
         } else if (use_mma(m, {L.q, L.k, L.v})) {
             CK_M(rmsnorm_launch(m->x, E, L.attn_nw, m->h, E, ntok, E, eps, st));
             const TensorMap *xh, *xl;
@@ -483,7 +487,8 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
         // x += Wo att
         if (gemv_supported(L.o->type, qd, ntok)) {
             GemvSegDesc so{L.o->d, nullptr, (int)L.o->type, E, EPI_ADD, m->x, E, nullptr, nullptr};
-            CK_M(gemv_launch(&so, 1, m->att, qd, qd, ntok, nullptr, eps, S, st));
+            const L2Range pf_f[2] = {{L.gate->d, (int64_t)L.gate->nbytes}, {L.up->d, (int64_t)L.up->nbytes}};
+            CK_M(gemv_launch(&so, 1, m->att, qd, qd, ntok, nullptr, eps, S, st, pf_f, 2));
         } else if (use_mma(m, {L.o})) {
             const TensorMap *xh, *xl;
             if (int rc = mma_split_x(m, m->att, qd, ntok, qd, &xh, &xl)) return rc;
@@ -497,7 +502,8 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
         if (gemv_supported(L.gate->type, E, ntok) && gemv_supported(L.up->type, E, ntok)) {
             if (pair) {
                 GemvSegDesc sf{L.gate->d, L.up->d, (int)L.gate->type, F, EPI_SWIGLU, m->hb, F, nullptr, nullptr};
-                CK_M(gemv_launch(&sf, 1, m->x, E, E, ntok, L.ffn_nw, eps, S, st));
+                const L2Range pf_d[1] = {{L.down->d, (int64_t)L.down->nbytes}};
+                CK_M(gemv_launch(&sf, 1, m->x, E, E, ntok, L.ffn_nw, eps, S, st, pf_d, 1));
             } else {
                 GemvSegDesc sf[2] = {{L.gate->d, nullptr, (int)L.gate->type, F, EPI_STORE, m->hb, F, nullptr, nullptr},
                                      {L.up->d, nullptr, (int)L.up->type, F, EPI_STORE, m->hb2, F, nullptr, nullptr}};
@@ -524,7 +530,16 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
         // x += Wd hb
         if (gemv_supported(L.down->type, F, ntok)) {
             GemvSegDesc sd{L.down->d, nullptr, (int)L.down->type, E, EPI_ADD, m->x, E, nullptr, nullptr};
-            CK_M(gemv_launch(&sd, 1, m->hb, F, F, ntok, nullptr, eps, S, st));
+            L2Range pf_n[3] = {};
+            int npf = 0;
+            if (l + 1 < c.n_layers) {
+                const Layer &N = m->layers[l + 1];
+                pf_n[0] = {N.q->d, (int64_t)N.q->nbytes};
+                pf_n[1] = {N.k->d, (int64_t)N.k->nbytes};
+                pf_n[2] = {N.v->d, (int64_t)N.v->nbytes};
+                npf = 3;
+            }
+            CK_M(gemv_launch(&sd, 1, m->hb, F, F, ntok, nullptr, eps, S, st, pf_n, npf));
         } else if (use_mma(m, {L.down})) {
             const TensorMap *xh, *xl;
             if (int rc = mma_split_x(m, m->hb, F, ntok, F, &xh, &xl)) return rc;
@@ -1656,14 +1671,17 @@ ACM_API int acm_model_bench_gemv(acm_model *m, int32_t reps, double *sec_per_pas
             GemvSegDesc sg[3] = {{L.q->d, nullptr, (int)L.q->type, qd, EPI_STORE, m->q, qd, L.q_b, nullptr},
                                  {L.k->d, nullptr, (int)L.k->type, kvd, EPI_STORE, m->k, kvd, L.k_b, nullptr},
                                  {L.v->d, nullptr, (int)L.v->type, kvd, EPI_STORE, m->v, kvd, L.v_b, nullptr}};
-            CK_M(gemv_launch(sg, 3, m->x, E, E, 1, L.attn_nw, eps, S, st));
+            const L2Range pf_o[1] = {{L.o->d, (int64_t)L.o->nbytes}};
+            CK_M(gemv_launch(sg, 3, m->x, E, E, 1, L.attn_nw, eps, S, st, pf_o, 1));
             B += (double)(L.q->nbytes + L.k->nbytes + L.v->nbytes) + 4.0 * (2 * E + qd + 2 * kvd);
             GemvSegDesc so{L.o->d, nullptr, (int)L.o->type, E, EPI_ADD, m->x, E, nullptr, nullptr};
-            CK_M(gemv_launch(&so, 1, m->att, qd, qd, 1, nullptr, eps, S, st));
+            const L2Range pf_f[2] = {{L.gate->d, (int64_t)L.gate->nbytes}, {L.up->d, (int64_t)L.up->nbytes}};
+            CK_M(gemv_launch(&so, 1, m->att, qd, qd, 1, nullptr, eps, S, st, pf_f, 2));
             B += (double)L.o->nbytes + 4.0 * (qd + 2 * E);
             if (L.gate->type == L.up->type) {
                 GemvSegDesc sf{L.gate->d, L.up->d, (int)L.gate->type, F, EPI_SWIGLU, m->hb, F, nullptr, nullptr};
-                CK_M(gemv_launch(&sf, 1, m->x, E, E, 1, L.ffn_nw, eps, S, st));
+                const L2Range pf_d[1] = {{L.down->d, (int64_t)L.down->nbytes}};
+                CK_M(gemv_launch(&sf, 1, m->x, E, E, 1, L.ffn_nw, eps, S, st, pf_d, 1));
             } else {
                 GemvSegDesc sf[2] = {{L.gate->d, nullptr, (int)L.gate->type, F, EPI_STORE, m->hb, F, nullptr, nullptr},
                                      {L.up->d, nullptr, (int)L.up->type, F, EPI_STORE, m->hb2, F, nullptr, nullptr}};
@@ -1671,7 +1689,16 @@ ACM_API int acm_model_bench_gemv(acm_model *m, int32_t reps, double *sec_per_pas
             }
             B += (double)(L.gate->nbytes + L.up->nbytes) + 4.0 * (2 * E + F);
             GemvSegDesc sd{L.down->d, nullptr, (int)L.down->type, E, EPI_ADD, m->x, E, nullptr, nullptr};
-            CK_M(gemv_launch(&sd, 1, m->hb, F, F, 1, nullptr, eps, S, st));
+            L2Range pf_n[3] = {};
+            int npf = 0;
+            if (l + 1 < c.n_layers) {
+                const Layer &N = m->layers[l + 1];
+                pf_n[0] = {N.q->d, (int64_t)N.q->nbytes};
+                pf_n[1] = {N.k->d, (int64_t)N.k->nbytes};
+                pf_n[2] = {N.v->d, (int64_t)N.v->nbytes};
+                npf = 3;
+            }
+            CK_M(gemv_launch(&sd, 1, m->hb, F, F, 1, nullptr, eps, S, st, pf_n, npf));
             B += (double)L.down->nbytes + 4.0 * (F + 2 * E);
             nl += 4;
         }

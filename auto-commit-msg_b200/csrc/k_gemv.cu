@@ -96,6 +96,15 @@ __global__ void __launch_bounds__(Cfg<MT>::NT, 1) k_gemv(const __grid_constant__
                 bulk_g2s(dst, s.w + a0, (uint32_t)(a1 - a0), &full[slot]);
                 if (s.w2) bulk_g2s(dst + (a1 - a0), s.w2 + c0, (uint32_t)(c1 - c0), &full[slot]);
             }
+            // this CTA's share of the next matvec's weights into L2
+            for (int i = 0; i < a.npf; i++) {
+                const int64_t bytes = a.pf[i].bytes;
+                const int64_t chunk = ((bytes + gridDim.x - 1) / gridDim.x + 15) & ~int64_t(15);
+                const int64_t off = (int64_t)blockIdx.x * chunk;
+                if (off >= bytes) continue;
+                const int64_t len = std::min<int64_t>(chunk, bytes - off) & ~int64_t(15);
+                if (len > 0) prefetch_l2(static_cast<const uint8_t *>(a.pf[i].p) + off, (uint32_t)len);
+            }
         }
         pdl_wait();
         return;
@@ -164,9 +173,13 @@ static cudaError_t launch_types(GemvArgs &a, int ta, int tb, int grid, size_t sm
 
 // One launch for segments whose types are {ta} or {ta, tb}.
 static cudaError_t gemv_launch_group(const GemvSegDesc *segs, int nseg, int ta, int tb, const float *x, int ldx,
-                                     int64_t k, int m, const float *norm_w, float eps, int num_sms, cudaStream_t st) {
+                                     int64_t k, int m, const float *norm_w, float eps, int num_sms, cudaStream_t st,
+                                     const L2Range *pf, int npf) {
     const int mt = mt_of(m);
     GemvArgs a{};
+    a.npf = 0;
+    for (int i = 0; i < npf && a.npf < GEMV_MAX_PF; i++)
+        if (pf[i].p && pf[i].bytes >= 16 && ((uintptr_t)pf[i].p & 15) == 0) a.pf[a.npf++] = pf[i];
     a.nseg = nseg;
     a.x = x;
     a.ldx = ldx;
@@ -263,7 +276,7 @@ static cudaError_t gemv_launch_group(const GemvSegDesc *segs, int nseg, int ta, 
 }
 
 cudaError_t gemv_launch(const GemvSegDesc *segs, int nseg, const float *x, int ldx, int64_t k, int m,
-                        const float *norm_w, float eps, int num_sms, cudaStream_t st) {
+                        const float *norm_w, float eps, int num_sms, cudaStream_t st, const L2Range *pf, int npf) {
     if (nseg < 1 || nseg > GEMV_MAX_SEG || m < 1 || m > 8) return cudaErrorInvalidValue;
     // common instance: every type equal, or exactly {Q4_K, Q6_K}
     bool same = true, q46 = true;
@@ -271,8 +284,9 @@ cudaError_t gemv_launch(const GemvSegDesc *segs, int nseg, const float *x, int l
         same &= segs[i].type == segs[0].type;
         q46 &= segs[i].type == T_Q4_K || segs[i].type == T_Q6_K;
     }
-    if (same) return gemv_launch_group(segs, nseg, segs[0].type, segs[0].type, x, ldx, k, m, norm_w, eps, num_sms, st);
-    if (q46) return gemv_launch_group(segs, nseg, T_Q4_K, T_Q6_K, x, ldx, k, m, norm_w, eps, num_sms, st);
+    if (same)
+        return gemv_launch_group(segs, nseg, segs[0].type, segs[0].type, x, ldx, k, m, norm_w, eps, num_sms, st, pf, npf);
+    if (q46) return gemv_launch_group(segs, nseg, T_Q4_K, T_Q6_K, x, ldx, k, m, norm_w, eps, num_sms, st, pf, npf);
     // otherwise one launch per distinct type (CTAs split by bytes)
     double tot = 0;
     for (int j = 0; j < nseg; j++) tot += (double)row_bytes(segs[j].type, k) * segs[j].n;
@@ -289,7 +303,7 @@ cudaError_t gemv_launch(const GemvSegDesc *segs, int nseg, const float *x, int l
             }
         const int sms = std::max(1, (int)(num_sms * frac / tot + 0.5));
         cudaError_t e = gemv_launch_group(grp.data(), (int)grp.size(), segs[i].type, segs[i].type, x, ldx, k, m,
-                                          norm_w, eps, sms, st);
+                                          norm_w, eps, sms, st, pf, npf);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

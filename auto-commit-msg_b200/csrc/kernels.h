@@ -40,6 +40,15 @@ struct GemvSeg {
 constexpr int GEMV_MAX_SEG = 4;
 constexpr int GEMV_NS_MAX = 8;
 
+// An HBM range pulled into L2 ahead of its use: the weights of the next
+// matvec, prefetched by this one's producer warps (split across its CTAs), so
+// the next kernel's first stages come from L2 instead of DRAM.
+struct L2Range {
+    const void *p;
+    int64_t bytes;
+};
+constexpr int GEMV_MAX_PF = 3;
+
 struct GemvArgs {
     GemvSeg seg[GEMV_MAX_SEG];
     int nseg;
@@ -53,6 +62,8 @@ struct GemvArgs {
     int stage_bytes;
     int stage_off;       // byte offset of the stage ring in shared memory
     int lpr;             // 0: one row per warp (unit path); else lanes per row (wide path)
+    L2Range pf[GEMV_MAX_PF];
+    int npf;
 };
 
 struct GemvSegDesc {
@@ -69,7 +80,8 @@ struct GemvSegDesc {
 // Plans CTA ranges / stages and launches (possibly several launches when the
 // segments' types have no common kernel instance).  Returns a cudaError_t.
 cudaError_t gemv_launch(const GemvSegDesc *segs, int nseg, const float *x, int ldx, int64_t k, int m,
-                        const float *norm_w, float eps, int num_sms, cudaStream_t st);
+                        const float *norm_w, float eps, int num_sms, cudaStream_t st, const L2Range *pf = nullptr,
+                        int npf = 0);
 bool gemv_supported(int type, int64_t k, int m);
 
 // Prefill / batched GEMM: y[m][n] (epi) x[m][k] . W[n][k]^T.

@@ -42,6 +42,24 @@ def test_forward_and_teacher_forced_decode(acm, eng, oracle, synth, tiny_models,
     m.close()
 
 
+@pytest.mark.parametrize("name", ["qwen3", "qwen2", "llama_f16"])
+def test_prefill_continues_context(acm, eng, oracle, synth, tiny_models, name):
+    """A prefill that continues earlier context (Forward of 70 tokens, then of
+    130 more at positions 70..199): the second chunk's attention reads keys
+    written by the first (the tensor-core attention's pos0 > 0 path, key
+    blocks that straddle the chunks, G query heads per kv head)."""
+    m = acm.Load(tiny_models[name], 0, engine=eng)
+    o = oracle.Model(tiny_models[name], 0)
+    p1 = synth.prompt_ids(70, m.Cfg.vocab, 17)
+    p2 = synth.prompt_ids(130, m.Cfg.vocab, 18)
+    assert rel_l2(m.Forward(p1), o.forward(p1)) < 1e-4
+    lg, lo = m.Forward(p2), o.forward(p2)
+    assert rel_l2(lg, lo) < 1e-4
+    assert int(np.argmax(lg)) == int(np.argmax(lo))
+    assert m.Pos() == o.pos == 200
+    m.close()
+
+
 @pytest.mark.parametrize("name", ARCHS)
 def test_generate_greedy_matches_oracle(acm, eng, oracle, synth, tiny_models, name):
     m = acm.Load(tiny_models[name], 0, engine=eng)
