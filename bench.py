@@ -285,6 +285,68 @@ def bench_gemv(acm, m, reps=20):
     return sec.value, b.value, nl.value
 
 
+SERVE_N, SERVE_GEN, SERVE_BATCH, SERVE_CTX = 512, 48, 64, 1152
+
+
+def serve_requests():
+    """The many-request workload: 512 prompts of U[300, 1000] uniform ids
+    (seed 5), per-request sampler seed 1000 + i, top-k 40, T 0.7, top-p off,
+    48 decode tokens each."""
+    import numpy as np
+    rng = np.random.default_rng(5)
+    lens = rng.integers(300, 1001, SERVE_N)
+    return [(rng.integers(0, 151936, int(n)).astype(np.int32), 1000 + i) for i, n in enumerate(lens)]
+
+
+def partition(reqs, world):
+    """Longest-prompt-first greedy balancing of (prompt + decode) work."""
+    load = [0] * world
+    parts = [[] for _ in range(world)]
+    for i in sorted(range(len(reqs)), key=lambda i: -len(reqs[i][0])):
+        r = min(range(world), key=lambda j: load[j])
+        parts[r].append(i)
+        load[r] += len(reqs[i][0]) + SERVE_GEN
+    return parts
+
+
+def run_serve(args, rank, world, local):
+    """512 independent requests, <= 64 sharing each decode step per GPU
+    (acm_serve), data parallel over the ranks; prints prefill and decode
+    aggregate tok/s (device time, max over ranks) and the wall-clock rate."""
+    import torch
+    acm = importlib.import_module("auto-commit-msg_b200")
+    path, _ = model_path(rank, world)
+    torch.cuda.set_device(local)
+    eng = acm.Engine(local)
+    m = acm.Load(path, SERVE_CTX, engine=eng, max_seqs=SERVE_BATCH + 1)
+    reqs = serve_requests()
+    mine = [reqs[i] for i in partition(reqs, world)[rank]]
+    batch = [(p, acm.Sampler(0.7, 40, 0.0, Seed=seed), SERVE_GEN) for p, seed in mine]
+    m.Serve(batch[: min(len(batch), 2 * SERVE_BATCH)], max_batch=SERVE_BATCH, stop_on_eos=False)  # warm-up
+    barrier(world)
+    torch.cuda.synchronize()
+    w0 = time.perf_counter()
+    res = m.Serve(batch, max_batch=SERVE_BATCH, stop_on_eos=False)
+    wall = time.perf_counter() - w0
+    st = m.Stats
+    bad = sum(1 for ids, status in res if status != 0 or len(ids) != SERVE_GEN)
+    tot = allreduce([float(st.PrefillToks), float(st.DecodeToks), float(bad)], world, "sum")
+    mx = allreduce([st.Prefill, st.Decode, wall], world, "max")
+    if rank == 0:
+        print(json.dumps({
+            "metric": "many-request serving: prefill & decode aggregate tok/s (Qwen3-0.6B-shape Q4_K_M)",
+            "value": round(tot[1] / mx[1], 1), "unit": "decode tok/s", "prefill_tok_s": round(tot[0] / mx[0], 1),
+            "n_gpus": world, "higher_is_better": True, "scaling": "strong",
+            "wall_tok_s": round(tot[1] / mx[2], 1), "wall_s": round(mx[2], 3), "failed_requests": int(tot[2]),
+            "config": {"workload": f"{SERVE_N} requests, prompts U[300,1000] (seed 5), {SERVE_GEN} decode tokens, "
+                                   f"top-k 40, T 0.7, seed 1000+i, <= {SERVE_BATCH} concurrent per GPU, "
+                                   "longest-prompt-first partition over GPUs",
+                       "prefill_tokens": int(tot[0]), "decode_tokens": int(tot[1])},
+            "data": "synthetic (random-init weights, seeded prompts)"}), flush=True)
+    m.close()
+    eng.close()
+
+
 def run_profile(args):
     """Short workloads for the profiler (no JSON line): `prefill` runs three
     389-token prefills; `decode` one prefill + `--tokens` greedy decode tokens;
@@ -342,6 +404,8 @@ def main():
     ap.add_argument("--profile", choices=["prefill", "decode", "trace"],
                     help="run a short workload for the profiler instead of the benchmark")
     ap.add_argument("--tokens", type=int, default=8, help="decode tokens of --profile decode/trace")
+    ap.add_argument("--workload", choices=["single", "serve"], default="single",
+                    help="single: the batch-1 Generate benchmark (default); serve: 512 requests through acm_serve")
     args = ap.parse_args()
     if args.profile:
         run_profile(args)
@@ -350,6 +414,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.workload == "serve":
+            run_serve(args, rank, world, local)
         else:
             run_ours(args, rank, world, local)
     finally:
