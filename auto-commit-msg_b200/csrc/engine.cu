@@ -892,14 +892,16 @@ ACM_API int acm_model_create(acm_engine *e, const acm_config *cfg, int32_t max_s
     return ACM_OK;
 }
 
-ACM_API int acm_model_add_tensor(acm_model *m, const char *name, uint32_t ggml_type, const uint64_t *dims,
-                                 int32_t ndims, const void *host_bytes, size_t nbytes) {
-    if (!m || !name || (ndims > 0 && !dims) || ndims < 0 || ndims > 8 || (!host_bytes && nbytes))
-        return set_err(m, ACM_ERR_INVALID, "invalid tensor arguments");
+}  // extern "C"
+
+namespace {
+// Shape checks of one GGUF tensor (the part of acm_model_add_tensor before
+// any device work); fills t.
+int tensor_meta(acm_model *m, const char *name, uint32_t ggml_type, const uint64_t *dims, int32_t ndims,
+                size_t nbytes, DevTensor &t) {
     if (m->finalized) return set_err(m, ACM_ERR_INVALID, "model already finalized");
     if (!type_ok((int)ggml_type))
         return set_err(m, ACM_ERR_UNSUPPORTED_TYPE, fmt("tensor %s: unsupported type %u", name, ggml_type));
-    DevTensor t;
     t.name = name;
     t.type = ggml_type;
     t.numel = 1;
@@ -913,6 +915,100 @@ ACM_API int acm_model_add_tensor(acm_model *m, const char *name, uint32_t ggml_t
     t.nbytes = (size_t)(t.numel / be) * blk_bytes((int)ggml_type);
     if (nbytes != t.nbytes)
         return set_err(m, ACM_ERR_INVALID, fmt("tensor %s: %zu bytes given, %zu expected", name, nbytes, t.nbytes));
+    return ACM_OK;
+}
+
+// Upload of a whole GGUF (the fast path of acm_model_load_gguf): one device
+// arena for every used tensor (256-byte aligned slots, 64 zero bytes after
+// each), filled through two pinned staging buffers -- the host copies the
+// next chunk out of the mmap while the copy engine moves the previous one.
+int upload_gguf(acm_model *m, const gguf::File &f, const std::vector<const std::string *> &names) {
+    cudaStream_t st = m->e->stream;
+    std::vector<DevTensor> ts(names.size());
+    std::vector<size_t> offs(names.size());
+    size_t total = 0;
+    for (size_t i = 0; i < names.size(); i++) {
+        const gguf::Tensor &t = f.tensors.at(*names[i]);
+        if (int rc = tensor_meta(m, names[i]->c_str(), t.type, t.dims.data(), (int)t.dims.size(), t.nbytes, ts[i]))
+            return rc;
+        offs[i] = total;
+        total += (t.nbytes + 64 + 255) & ~size_t(255);
+    }
+    uint8_t *arena = nullptr;
+    CK_M(dalloc(m, &arena, total));
+    constexpr size_t CH = 64u << 20;
+    uint8_t *stage[2] = {nullptr, nullptr};
+    cudaEvent_t done[2] = {nullptr, nullptr};
+    int rc = ACM_OK;
+    for (int b = 0; b < 2 && !rc; b++) {
+        if (cudaMallocHost(reinterpret_cast<void **>(&stage[b]), CH) != cudaSuccess ||
+            cudaEventCreateWithFlags(&done[b], cudaEventDisableTiming) != cudaSuccess)
+            rc = set_err(m, ACM_ERR_OOM, "pinned staging buffer");
+    }
+    // the arena's bytes in order, CH at a time: tensor bytes from the mmap,
+    // zeros for the padding after each tensor
+    bool pending[2] = {false, false};
+    size_t ti = 0;
+    int b = 0;
+    for (size_t pos = 0; pos < total && !rc; pos += CH) {
+        if (pending[b]) {
+            cudaError_t e = cudaEventSynchronize(done[b]);  // staging buffer b free again
+            if (e != cudaSuccess) {
+                rc = set_err(m, ACM_ERR_CUDA, fmt("upload: %s", cudaGetErrorString(e)));
+                break;
+            }
+        }
+        const size_t n = std::min(CH, total - pos);
+        for (size_t q = 0; q < n;) {
+            const size_t at = pos + q;
+            while (ti + 1 < names.size() && offs[ti + 1] <= at) ti++;
+            const gguf::Tensor &t = f.tensors.at(*names[ti]);
+            const size_t end_t = offs[ti] + t.nbytes, end_slot = ti + 1 < names.size() ? offs[ti + 1] : total;
+            if (at < end_t) {
+                const size_t c = std::min(end_t - at, n - q);
+                memcpy(stage[b] + q, static_cast<const uint8_t *>(t.data) + (at - offs[ti]), c);
+                q += c;
+            } else {
+                const size_t c = std::min(end_slot - at, n - q);
+                memset(stage[b] + q, 0, c);
+                q += c;
+            }
+        }
+        if (cudaMemcpyAsync(arena + pos, stage[b], n, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            cudaEventRecord(done[b], st) != cudaSuccess) {
+            rc = set_err(m, ACM_ERR_CUDA, "upload copy failed");
+            break;
+        }
+        pending[b] = true;
+        b ^= 1;
+    }
+    if (!rc) {
+        cudaError_t e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) rc = set_err(m, ACM_ERR_CUDA, fmt("upload: %s", cudaGetErrorString(e)));
+    } else {
+        cudaStreamSynchronize(st);  // no copy may still read a staging buffer
+    }
+    for (int k = 0; k < 2; k++) {
+        if (done[k]) cudaEventDestroy(done[k]);
+        if (stage[k]) cudaFreeHost(stage[k]);
+    }
+    if (rc) return rc;
+    for (size_t i = 0; i < names.size(); i++) {
+        ts[i].d = arena + offs[i];
+        m->tensors[*names[i]] = std::move(ts[i]);
+    }
+    return ACM_OK;
+}
+}  // namespace
+
+extern "C" {
+
+ACM_API int acm_model_add_tensor(acm_model *m, const char *name, uint32_t ggml_type, const uint64_t *dims,
+                                 int32_t ndims, const void *host_bytes, size_t nbytes) {
+    if (!m || !name || (ndims > 0 && !dims) || ndims < 0 || ndims > 8 || (!host_bytes && nbytes))
+        return set_err(m, ACM_ERR_INVALID, "invalid tensor arguments");
+    DevTensor t;
+    if (int rc = tensor_meta(m, name, ggml_type, dims, ndims, nbytes, t)) return rc;
     cudaSetDevice(m->e->device);
     // 16 bytes of padding: the bulk copies round spans up to 16 bytes and the
     // unaligned word loader reads one word past a run
@@ -1152,14 +1248,13 @@ ACM_API int acm_model_load_gguf(acm_engine *e, const char *path, int32_t max_ctx
         munmap(map, len);
         return rc;
     }
-    for (const std::string &name : f.order) {
-        const gguf::Tensor &t = f.tensors[name];
-        const bool used = name == "token_embd.weight" || name == "output.weight" || name == "output_norm.weight" ||
-                          name.rfind("blk.", 0) == 0;
-        if (!used) continue;
-        rc = acm_model_add_tensor(m, name.c_str(), t.type, t.dims.data(), (int)t.dims.size(), t.data, t.nbytes);
-        if (rc) break;
-    }
+    std::vector<const std::string *> names;
+    for (const std::string &name : f.order)
+        if (name == "token_embd.weight" || name == "output.weight" || name == "output_norm.weight" ||
+            name.rfind("blk.", 0) == 0)
+            names.push_back(&name);
+    cudaSetDevice(e->device);
+    rc = upload_gguf(m, f, names);
     munmap(map, len);
     if (!rc) rc = acm_model_finalize(m);
     if (rc) {

@@ -360,6 +360,16 @@ def run_profile(args):
     lib = acm.lib()
     path, prompt = model_path(0, 1)
     eng = acm.Engine(0)
+    if args.profile == "load":
+        for i in range(3):  # GGUF parse + upload of every tensor + finalize, wall clock
+            t0 = time.perf_counter()
+            m = acm.Load(path, CTX, engine=eng)
+            eng.sync()
+            print(f"load {i}: {1e3 * (time.perf_counter() - t0):.1f} ms ({os.path.getsize(path) / 2**20:.0f} MiB file)",
+                  flush=True)
+            m.close()
+        eng.close()
+        return
     m = acm.Load(path, CTX, engine=eng)
     if args.profile == "prefill":
         for i in range(3):
@@ -401,7 +411,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--profile", choices=["prefill", "decode", "trace"],
+    ap.add_argument("--profile", choices=["prefill", "decode", "trace", "load"],
                     help="run a short workload for the profiler instead of the benchmark")
     ap.add_argument("--tokens", type=int, default=8, help="decode tokens of --profile decode/trace")
     ap.add_argument("--workload", choices=["single", "serve"], default="single",
