@@ -106,8 +106,8 @@ __device__ __forceinline__ void dec_item_offsets(const KVDesc &kv, int seq, int 
 // Latency is what matters at this size (a few KB per item): the cached rows
 // are requested first, every other global load is issued before any is
 // consumed, and the merge pulls whole partial rows into shared memory with
-// asynchronous copies (one round trip per head for up to
-// (CH*(HD+4) + CH*HD) / (HD+4) slices).  Register use stays small so the
+// asynchronous copies (one round trip for every head's rows while G x slices
+// fits (CH*(HD+4) + CH*HD) / (HD+4) rows, else per head in tiles).  Register use stays small so the
 // item also runs inside the persistent decode kernel's 96-register budget.
 template <int HD, int CH>
 __device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const float *k_nw, const AttnDesc &a,
@@ -137,11 +137,10 @@ __device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const flo
     {
         constexpr int CPR = HD / 4;  // 16-byte pieces per row
         const float *kb = kv.k + lofs + base, *vb = kv.v + lofs + base;
-        for (int i = gtid; i < ncopy * CPR * 2; i += 128) {
-            const int which = i / (ncopy * CPR), rem = i - which * ncopy * CPR;
-            const int p = rem / CPR, piece = rem - p * CPR;
-            if (which) cp_async16(vs + p * HD + piece * 4, vb + (int64_t)p * kv.kvd + piece * 4);
-            else cp_async16(ks + p * KS + piece * 4, kb + (int64_t)p * kv.kvd + piece * 4);
+        for (int i = gtid; i < ncopy * CPR; i += 128) {  // K and V piece together, constant divisors
+            const int p = i / CPR, piece = i - p * CPR;
+            cp_async16(ks + p * KS + piece * 4, kb + (int64_t)p * kv.kvd + piece * 4);
+            cp_async16(vs + p * HD + piece * 4, vb + (int64_t)p * kv.kvd + piece * 4);
         }
     }
     // ---- query heads (and the new key): loads, then norm + rope ----
@@ -264,9 +263,45 @@ __device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const flo
     named_sync(bid, 128);
     if (*flag) {
         __threadfence();
-        // merge buffer: the ks..vs region, `cap` partial rows at a time
+        // merge buffer: the ks..vs region, CAP partial rows at a time
         float *buf = ks;
         constexpr int CAP = (CH * KS + CH * HD) / PS;
+        if (G * nchunk <= CAP) {
+            // every head's partial rows in one round of copies
+            for (int h = 0; h < G; h++) {
+                const float *ph = a.part + ((int64_t)t * nh + g * G + h) * a.nsplit * PS;
+                float *bh = buf + h * nchunk * PS;
+                for (int i = gtid; i < nchunk * (PS / 4); i += 128) {
+                    const int cc = i / (PS / 4), piece = i - cc * (PS / 4);
+                    cp_async16(bh + cc * PS + piece * 4, ph + (int64_t)cc * PS + piece * 4);
+                }
+            }
+            cp_async_wait_all();
+            named_sync(bid, 128);
+            for (int h = 0; h < G; h++) {
+                const float *bh = buf + h * nchunk * PS;
+                float M = -FLT_MAX, num = 0.f, den = 0.f;
+                for (int cc = 0; cc < nchunk; cc++) M = fmaxf(M, bh[cc * PS + HD]);
+                for (int cc = gp; cc < nchunk; cc += GROUPS) {
+                    const float w = fast_exp(bh[cc * PS + HD] - M);
+                    num = fmaf(w, bh[cc * PS + d], num);
+                    den = fmaf(w, bh[cc * PS + HD + 1], den);
+                }
+                if (GROUPS > 1) {
+                    if (gp > 0) {
+                        gred[d] = num;
+                        if (d == 0) stat[0] = den;
+                    }
+                    named_sync(bid, 128);
+                    if (gp == 0) {
+                        num += gred[d];
+                        den += stat[0];
+                    }
+                    named_sync(bid, 128);
+                }
+                if (gp == 0) a.out[(int64_t)t * qd + (int64_t)(g * G + h) * HD + d] = num / den;
+            }
+        } else
         for (int h = 0; h < G; h++) {
             const float *ph = a.part + ((int64_t)t * nh + g * G + h) * a.nsplit * PS;
             float M = -FLT_MAX, num = 0.f, den = 0.f;
