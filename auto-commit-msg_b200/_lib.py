@@ -78,6 +78,8 @@ SIGNATURES = {
     "acm_dequant": (C.c_int, [P, C.c_uint32, P, C.c_int64, C.c_int64, P]),
     "acm_matmul": (C.c_int, [P, C.c_uint32, P, C.c_int64, C.c_int64, P, C.c_int32, P]),
     "acm_matmul_dev": (C.c_int, [P, C.c_uint32, P, C.c_int64, C.c_int64, P, C.c_int32, P]),
+    "acm_bench_matmul": (C.c_int, [P, C.c_uint32, P, C.c_int64, C.c_int32, C.c_int64, C.c_int64, P, C.c_int32, P,
+                                   C.c_int32, C.POINTER(C.c_double)]),
     "acm_sample_logits": (C.c_int, [P, P, C.c_int32, C.POINTER(CSampler), C.c_uint64, C.POINTER(C.c_int32)]),
     "acm_sample_dev_noalloc": (C.c_int, [P, P, C.c_int64, C.c_int32, C.c_int32, P, P, P]),
     "acm_engine_stream": (P, [P]),

@@ -1909,7 +1909,9 @@ ACM_API int acm_matmul_dev(acm_engine *e, uint32_t ggml_type, const void *d_w, i
     } else if (k % 64 == 0 && mma_available()) {
         // tensor-core path: split W and x to bf16 hi/lo in the second scratch
         const size_t wbs = al256((size_t)rows64(n) * k * 2), xbs = al256((size_t)rows64(m) * k * 2);
-        const size_t wsf = 4 * (size_t)m * n;  // split-K partial sums
+        // split-K partial sums: split-K runs only when the tiles fill at most
+        // half the SMs, so ks * m * n stays within 148 tiles of 128 x 64
+        const size_t wsf = std::min<size_t>(4 * (size_t)m * n, (size_t)148 * 128 * 64);
         uint8_t *s2 = nullptr;
         if (int rc = scratch2(e, 2 * wbs + 2 * xbs + wsf * 4, &s2)) return rc;
         uint8_t *whi = s2, *wlo = s2 + wbs, *xhi = s2 + 2 * wbs, *xlo = xhi + xbs;
@@ -1927,6 +1929,37 @@ ACM_API int acm_matmul_dev(acm_engine *e, uint32_t ggml_type, const void *d_w, i
                          e->stream));
     }
     return ACM_OK;
+}
+
+ACM_API int acm_bench_matmul(acm_engine *e, uint32_t ggml_type, const void *d_w, int64_t w_stride, int32_t copies,
+                             int64_t n, int64_t k, const float *d_x, int32_t m, float *d_y, int32_t reps,
+                             double *sec_per_call) {
+    if (!e || !d_w || !sec_per_call || copies <= 0 || reps <= 0 || w_stride < 0 || w_stride % 256)
+        return ACM_ERR_INVALID;
+    if (copies > 1 && w_stride < (int64_t)n * row_bytes((int)ggml_type, k) + 16)
+        return set_eerr(e, ACM_ERR_INVALID, "weight copies overlap");
+    cudaSetDevice(e->device);
+    const uint8_t *w0 = static_cast<const uint8_t *>(d_w);
+    for (int i = 0; i < copies; i++)  // untimed pass over every copy
+        if (int rc = acm_matmul_dev(e, ggml_type, w0 + (int64_t)i * w_stride, n, k, d_x, m, d_y)) return rc;
+    cudaEvent_t ev[2];
+    CK_E(cudaEventCreate(&ev[0]));
+    if (cudaEventCreate(&ev[1]) != cudaSuccess) {
+        cudaEventDestroy(ev[0]);
+        return set_eerr(e, ACM_ERR_CUDA, "cudaEventCreate failed");
+    }
+    int rc = ACM_OK;
+    float ms = 0.f;
+    if (cudaEventRecord(ev[0], e->stream) != cudaSuccess) rc = set_eerr(e, ACM_ERR_CUDA, "cudaEventRecord failed");
+    for (int i = 0; i < reps && rc == ACM_OK; i++)
+        rc = acm_matmul_dev(e, ggml_type, w0 + (int64_t)(i % copies) * w_stride, n, k, d_x, m, d_y);
+    if (rc == ACM_OK && (cudaEventRecord(ev[1], e->stream) != cudaSuccess || cudaEventSynchronize(ev[1]) != cudaSuccess ||
+                         cudaEventElapsedTime(&ms, ev[0], ev[1]) != cudaSuccess))
+        rc = set_eerr(e, ACM_ERR_CUDA, cudaGetErrorString(cudaGetLastError()));
+    cudaEventDestroy(ev[0]);
+    cudaEventDestroy(ev[1]);
+    if (rc == ACM_OK) *sec_per_call = 1e-3 * ms / reps;
+    return rc;
 }
 
 ACM_API int acm_matmul(acm_engine *e, uint32_t ggml_type, const void *host_w, int64_t n, int64_t k,

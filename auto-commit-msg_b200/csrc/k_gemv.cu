@@ -212,7 +212,14 @@ static cudaError_t gemv_launch_group(const GemvSegDesc *segs, int nseg, int ta, 
         sb = std::max<int64_t>(sb, (((int64_t)ncw * (32 / a.lpr) * maxrow + 64 + 127) / 128) * 128);
     }
     int ns = (int)std::min<int64_t>(6, ((int64_t)SMEM_MAX - (int64_t)xb - 16) / sb);
-    if (ns < 2) {
+    if (ns < 2 && a.lpr) {
+        // long rows (Q8_0 / F16 at K >= 1024): two stages as large as shared
+        // memory allows; the stage then feeds fewer warps, but the ring stays
+        // double-buffered (one-row stages serialise the copies row by row)
+        sb = (((int64_t)SMEM_MAX - (int64_t)xb - 16) / 2) & ~int64_t(127);
+        ns = 2;
+    }
+    if (ns < 2 || sb < maxrow + 64) {
         sb = ((maxrow + 64 + 127) / 128) * 128;
         ns = (int)std::min<int64_t>(GEMV_NS_MAX, ((int64_t)SMEM_MAX - (int64_t)xb - 16) / sb);
         if (ns < 2) return cudaErrorInvalidValue;

@@ -92,6 +92,15 @@ class Engine:
         self._check(_lib.lib().acm_matmul_dev(self._h, typ, C.c_void_p(d_w), n, k, C.c_void_p(d_x), m,
                                               C.c_void_p(d_y)))
 
+    def bench_matmul(self, typ: int, d_w: int, w_stride: int, copies: int, n: int, k: int, d_x: int, m: int,
+                     d_y: int, reps: int) -> float:
+        """Mean device seconds of one matmul_dev call over `reps` back-to-back
+        calls cycling through `copies` weight copies (acm_bench_matmul)."""
+        sec = C.c_double()
+        self._check(_lib.lib().acm_bench_matmul(self._h, typ, C.c_void_p(d_w), w_stride, copies, n, k,
+                                                C.c_void_p(d_x), m, C.c_void_p(d_y), reps, C.byref(sec)))
+        return sec.value
+
     def sample_logits(self, logits: np.ndarray, s: Sampler, step: int) -> int:
         lg = np.ascontiguousarray(logits, dtype=np.float32)
         out = C.c_int32(-1)

@@ -347,6 +347,85 @@ def run_serve(args, rank, world, local):
     eng.close()
 
 
+KB_TYPES = {"q4_0": 2, "q5_0": 6, "q8_0": 8, "q4_k": 12, "q5_k": 13, "q6_k": 14}
+KB_SHAPES = [(1024, 2048), (2048, 1024), (1024, 3072), (3072, 1024), (1024, 151936)]  # [K x N]
+KB_M = (1, 389, 944)
+L2_BYTES = 126 * 2**20
+
+
+def kb_weights(synth, typ, k, n, seed, uniq=509):
+    """[N rows of K] weight bytes: `uniq` distinct quantized N(0, 0.02) rows
+    repeated over all N rows (quantizing 155M elements per type would take
+    longer than the bench itself; the kernels' time does not depend on the
+    values)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    one = np.frombuffer(synth.quantize(typ, rng.standard_normal((uniq, k)).astype(np.float32) * 0.02), np.uint8)
+    return np.tile(one, -(-n // uniq))[: n * synth.row_bytes(typ, k)]
+
+
+def run_kernels(args, rank, world, local):
+    """The kernel microbench: acm_matmul_dev for every quantized type x
+    [K x N] weight shape of the decode/prefill linears and the lm_head, at
+    M = 1 (fused dequant-GEMV) and M = 389 / 944 (tensor-core GEMM, the call
+    including the dequant + bf16 split of W and x).  L2 is defeated by
+    rotating weight copies totalling more than 2 x L2.  GB/s = weight bytes
+    per call / time (the reference's matvec bench definition)."""
+    import numpy as np
+    import torch
+    acm = importlib.import_module("auto-commit-msg_b200")
+    synth = importlib.import_module("auto-commit-msg_b200.synth")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    eng = acm.Engine(local)
+    peak, peak_kind = peaks()
+    tpk, tpk_kind = tensor_peak()
+    gen = torch.Generator(device=dev).manual_seed(2)
+    rows = []
+    n0 = acm.lib().acm_kernel_launches()
+    for tname, typ in KB_TYPES.items():
+        for k, n in KB_SHAPES:
+            w = kb_weights(synth, typ, k, n, seed=typ * 1000 + k + n)
+            wbytes = w.size
+            stride = (wbytes + 16 + 255) // 256 * 256
+            copies = max(8, -(-2 * L2_BYTES // wbytes) + 1)
+            buf = torch.empty(copies * stride, dtype=torch.uint8, device=dev)
+            wt = torch.from_numpy(w).to(dev)
+            for c in range(copies):
+                buf[c * stride: c * stride + wbytes].copy_(wt)
+            buf_view = buf.view(copies, stride)
+            buf_view[:, wbytes:].zero_()
+            del wt
+            for m in KB_M:
+                x = torch.randn(m, k, device=dev, generator=gen)
+                y = torch.empty(m, n, device=dev)
+                reps = max(2 * copies, 64) if m == 1 else max(copies, 8)
+                torch.cuda.synchronize()
+                sec = eng.bench_matmul(typ, buf.data_ptr(), stride, copies, n, k, x.data_ptr(), m, y.data_ptr(), reps)
+                r = {"type": tname, "K": k, "N": n, "M": m, "us": round(sec * 1e6, 2),
+                     "weight_GBs": round(wbytes / sec / 1e9, 1), "copies": copies}
+                if m == 1:
+                    r["hbm_frac"] = round(wbytes / sec / 1e9 / peak, 4)
+                else:
+                    r["useful_TFLOPs"] = round(2.0 * m * n * k / sec / 1e12, 2)
+                rows.append(r)
+                del x, y
+            del buf, buf_view
+            torch.cuda.empty_cache()
+    launches = acm.lib().acm_kernel_launches() - n0
+    if rank == 0:
+        print(json.dumps({
+            "metric": "kernel microbench: matmul weight GB/s (mvbench_test.go:30) and GEMM TFLOP/s, L2 defeated",
+            "unit": "GB/s", "higher_is_better": True, "n_gpus": 1, "rows": rows,
+            "peak": {"hbm_gbs": peak, "kind": peak_kind, "bf16_tflops": tpk, "bf16_kind": tpk_kind},
+            "config": {"workload": "6 quantized types x [K x N] in {1024x2048, 2048x1024, 1024x3072, 3072x1024, "
+                                   "1024x151936} x M in {1, 389, 944}",
+                       "l2": "rotating weight copies totalling > 2 x 126 MB L2",
+                       "gemm": "M > 8 calls include the dequant + bf16 hi/lo split of W (the model caches it)"},
+            "gpu_launches": int(launches), "data": "synthetic (509 distinct quantized rows, repeated)"}), flush=True)
+    eng.close()
+
+
 def run_profile(args):
     """Short workloads for the profiler (no JSON line): `prefill` runs three
     389-token prefills; `decode` one prefill + `--tokens` greedy decode tokens;
@@ -358,6 +437,29 @@ def run_profile(args):
 
     acm = importlib.import_module("auto-commit-msg_b200")
     lib = acm.lib()
+    if args.profile == "gemv":
+        # the lm_head-shape matvec ([K x N] = 1024 x 151936, M = 1) of one
+        # weight type, 6 calls over 4 weight copies (the first 3 warm up)
+        import torch
+        synth = importlib.import_module("auto-commit-msg_b200.synth")
+        typ = KB_TYPES[args.type]
+        k, n = 1024, 151936
+        w = kb_weights(synth, typ, k, n, seed=typ)
+        stride = (w.size + 16 + 255) // 256 * 256
+        buf = torch.zeros(4 * stride, dtype=torch.uint8, device="cuda:0")
+        wt = torch.from_numpy(w).cuda()
+        for c in range(4):
+            buf[c * stride: c * stride + w.size].copy_(wt)
+        x, y = torch.randn(1, k, device="cuda:0"), torch.empty(1, n, device="cuda:0")
+        eng = acm.Engine(0)
+        torch.cuda.synchronize()
+        for i in range(6):
+            eng.matmul_dev(typ, buf.data_ptr() + (i % 4) * stride, n, k, x.data_ptr(), 1, y.data_ptr())
+        eng.sync()
+        sec = eng.bench_matmul(typ, buf.data_ptr(), stride, 4, n, k, x.data_ptr(), 1, y.data_ptr(), 64)
+        print(f"gemv {args.type} {k}x{n}: {sec * 1e6:.2f} us, {w.size / sec / 1e9:.1f} GB/s", flush=True)
+        eng.close()
+        return
     path, prompt = model_path(0, 1)
     eng = acm.Engine(0)
     if args.profile == "load":
@@ -411,11 +513,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--profile", choices=["prefill", "decode", "trace", "load"],
+    ap.add_argument("--profile", choices=["prefill", "decode", "trace", "load", "gemv"],
                     help="run a short workload for the profiler instead of the benchmark")
     ap.add_argument("--tokens", type=int, default=8, help="decode tokens of --profile decode/trace")
-    ap.add_argument("--workload", choices=["single", "serve"], default="single",
-                    help="single: the batch-1 Generate benchmark (default); serve: 512 requests through acm_serve")
+    ap.add_argument("--type", choices=list(KB_TYPES), default="q4_k", help="weight type of --profile gemv")
+    ap.add_argument("--workload", choices=["single", "serve", "kernels"], default="single",
+                    help="single: the batch-1 Generate benchmark (default); serve: 512 requests through acm_serve; "
+                         "kernels: the matmul microbench over every quantized type and weight shape")
     args = ap.parse_args()
     if args.profile:
         run_profile(args)
@@ -426,6 +530,8 @@ def main():
             run_reference(args, rank, world)
         elif args.workload == "serve":
             run_serve(args, rank, world, local)
+        elif args.workload == "kernels":
+            run_kernels(args, rank, world, local)
         else:
             run_ours(args, rank, world, local)
     finally:

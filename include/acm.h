@@ -198,6 +198,18 @@ ACM_API int acm_matmul(acm_engine *e, uint32_t ggml_type, const void *host_w, in
 ACM_API int acm_matmul_dev(acm_engine *e, uint32_t ggml_type, const void *d_w, int64_t n, int64_t k,
                            const float *d_x, int32_t m, float *d_y);
 
+/* Kernel bench of acm_matmul_dev, the measurement of the reference's
+ * matvec bench (internal/infer/mvbench_test.go:12-33; GB/s = weight bytes
+ * over the time of one call, :30): `copies` copies of the weight tensor
+ * lie at d_w + i * w_stride (w_stride a multiple of 256; the copies together
+ * larger than L2, so that every call reads its weights from HBM).  One
+ * untimed call per copy, then `reps` calls back to back on the engine stream,
+ * call i on copy i % copies, timed with CUDA events around the sequence;
+ * sec_per_call = mean device seconds per call.  Synchronises the stream. */
+ACM_API int acm_bench_matmul(acm_engine *e, uint32_t ggml_type, const void *d_w, int64_t w_stride, int32_t copies,
+                             int64_t n, int64_t k, const float *d_x, int32_t m, float *d_y, int32_t reps,
+                             double *sec_per_call);
+
 /* Sample from host logits with the device sampler (sampler parity tests). */
 ACM_API int acm_sample_logits(acm_engine *e, const float *host_logits, int32_t n, const acm_sampler *s,
                               uint64_t step, int32_t *tok_out);

@@ -101,6 +101,49 @@ def test_microbench_shapes(eng, oracle, synth, typ, shape):
     _check_matmul(eng, oracle, synth, typ, n, k, 1, seed=k * 7 + n + typ)
 
 
+@pytest.mark.parametrize("typ", QTYPES)
+def test_microbench_lm_head_shape(eng, oracle, synth, typ):
+    """[K x N] = 1024 x 151936 (the tied lm_head) at batch 1: 509 distinct
+    quantized rows repeated over all 151936 rows (a prime period, so a row
+    index off by anything but a multiple of 509 shows)."""
+    k, n, u = 1024, 151936, 509
+    rng = np.random.default_rng(typ + 77)
+    one = synth.quantize(typ, rng.standard_normal((u, k)).astype(np.float32) * 0.02)
+    reps = -(-n // u)
+    w = (one * reps)[: n * synth.row_bytes(typ, k)]
+    x = rng.standard_normal((1, k)).astype(np.float32)
+    got = eng.matmul(typ, w, n, k, x)
+    yu = x.astype(np.float64) @ oracle.dequant(typ, one, u, k).astype(np.float64).T
+    want = np.tile(yu, (1, reps))[:, :n]
+    assert rel_l2(got, want) < 2e-6
+
+
+@pytest.mark.parametrize("typ,m", [(12, 1), (14, 1), (8, 389)])
+def test_bench_matmul_rotates_copies(eng, oracle, synth, typ, m):
+    """acm_bench_matmul: every call reads its own weight copy; the last call's
+    output is the product with copy (reps - 1) % copies."""
+    import torch
+    k, n, copies, reps = 1024, 300, 3, 5
+    rng = np.random.default_rng(typ + m)
+    ws = [synth.quantize(typ, rng.standard_normal((n, k)).astype(np.float32) * 0.02) for _ in range(copies)]
+    wb = len(ws[0])
+    stride = (wb + 16 + 255) // 256 * 256
+    buf = torch.zeros(copies * stride, dtype=torch.uint8, device="cuda:0")
+    for c, w in enumerate(ws):
+        buf[c * stride: c * stride + wb].copy_(torch.from_numpy(np.frombuffer(w, np.uint8).copy()))
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.empty(m, n, device="cuda:0")
+    torch.cuda.synchronize()
+    sec = eng.bench_matmul(typ, buf.data_ptr(), stride, copies, n, k, dx.data_ptr(), m, dy.data_ptr(), reps)
+    assert sec > 0
+    last = ws[(reps - 1) % copies]
+    want = x.astype(np.float64) @ oracle.dequant(typ, last, n, k).astype(np.float64).T
+    assert rel_l2(dy.cpu().numpy(), want) < (MMA_TOL if m > 8 else 2e-6)
+    with pytest.raises(Exception):  # overlapping copies are refused
+        eng.bench_matmul(typ, buf.data_ptr(), 256, copies, n, k, dx.data_ptr(), m, dy.data_ptr(), reps)
+
+
 def _logits(v, seed, ties=True):
     rng = np.random.default_rng(seed)
     lg = rng.standard_normal(v).astype(np.float32) * 2
