@@ -84,6 +84,28 @@ __host__ __device__ constexpr int dec_item_floats(int HD, int CH, int G) {
     return (G * (HD + 4) + CH * (HD + 4) + CH * HD + G * CH + 2 * G + (HD < 128 ? HD : 0) + 4 + 3) & ~3;
 }
 
+// Partial rows the merge buffer of an item holds (its K and V staging area).
+__host__ __device__ constexpr int dec_merge_rows(int HD, int CH) {
+    return (CH * (HD + 4) + CH * HD) / dec_part_stride(HD);
+}
+
+// Query heads per decode attention item: a divisor h of the group size G
+// whose partial rows (h x nch slices) fit the merge buffer in one round of
+// copies.  Among those, the largest that still gives at least min_items
+// items (nkv x nch x G/h), else the smallest; min_items 0 takes the largest.
+// Splitting a group over items re-reads its K/V rows (from L2) but lets
+// several CTAs merge at once, each over fewer rows.
+__host__ __device__ inline int dec_heads_per_item(int G, int nch, int nkv, int HD, int CH, int min_items) {
+    const int cap = dec_merge_rows(HD, CH);
+    int small = 0;
+    for (int h = G; h >= 1; h--) {
+        if (G % h || h * nch > cap) continue;
+        if (min_items <= 0 || nkv * nch * (G / h) >= min_items) return h;
+        small = h;
+    }
+    return small ? small : 1;
+}
+
 // Cache offsets of a decode attention item, without the layer term: `base`
 // of the slice's first position (the slice lies in one page, CH dividing the
 // page size) and `newo` of the new position `pos`; both include kv head g.
@@ -94,25 +116,29 @@ __device__ __forceinline__ void dec_item_offsets(const KVDesc &kv, int seq, int 
     newo = ((int64_t)pt[pos / kv.page_size] * kv.page_size + (pos % kv.page_size)) * kv.kvd + g * hd;
 }
 
-// One decode attention item: token t (new position pos), kv head g,
-// positions [c*CH, c*CH + CH) -- model.go:362-408 for that slice,
-// flash-decoding style -- run by 128 threads (gtid 0..127) that synchronise
-// on named barrier `bid`.  The item whose slice holds `pos` also normalises,
-// ropes and appends the new key/value (model.go:362-382).  With more than one
-// slice, each writes an unnormalised partial (sum e*v, max, sum e) and the
-// last slice of (t, g) to finish merges them.  sm: dec_item_floats(HD, CH,
-// G) floats, 16-byte aligned.  base / newo: dec_item_offsets.
+// One decode attention item: token t (new position pos), query heads
+// g*G + h0 .. g*G + h0 + hn - 1 of kv head g, positions [c*CH, c*CH + CH) --
+// model.go:362-408 for that slice, flash-decoding style -- run by 128 threads
+// (gtid 0..127) that synchronise on named barrier `bid`.  The items whose
+// slice holds `pos` also normalise and rope the new key (model.go:362-382);
+// the one with h0 == 0 appends key and value to the cache.  With more than
+// one slice, each writes an unnormalised partial (sum e*v, max, sum e) per
+// head and the last slice of (t, g, h0) to finish merges them.  sm:
+// dec_item_floats(HD, CH, G) floats, 16-byte aligned.  base / newo:
+// dec_item_offsets.
 //
 // Latency is what matters at this size (a few KB per item): the cached rows
 // are requested first, every other global load is issued before any is
 // consumed, and the merge pulls whole partial rows into shared memory with
-// asynchronous copies (one round trip for every head's rows while G x slices
-// fits (CH*(HD+4) + CH*HD) / (HD+4) rows, else per head in tiles).  Register use stays small so the
-// item also runs inside the persistent decode kernel's 96-register budget.
+// asynchronous copies (one round trip for every head's rows while hn x
+// slices fits dec_merge_rows, else per head in tiles); per-head maxima and
+// weights are warp reductions, the outputs one (head, dim) per thread.
+// Register use stays small so the item also runs inside the persistent
+// decode kernel's 96-register budget.
 template <int HD, int CH>
 __device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const float *k_nw, const AttnDesc &a,
                                  const KVDesc &kv, int layer, int t, int pos, int g, int c, int64_t base,
-                                 int64_t newo, float *sm, int gtid, int bid) {
+                                 int64_t newo, float *sm, int gtid, int bid, int h0, int hn) {
     constexpr int PER = HD / 32, QS = HD + 4, KS = HD + 4, NR = (HD / 2 + 31) / 32;
     constexpr int GROUPS = 128 / HD, PS = dec_part_stride(HD);
     static_assert(CH == 16 || CH == 32, "chunk must be 16 or 32 positions");
@@ -120,7 +146,7 @@ __device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const flo
     const int G = a.n_head / a.n_head_kv, nh = a.n_head, qd = nh * HD, kvd = a.n_head_kv * HD;
     const int L = pos + 1, lo = c * CH, hi = min(L, lo + CH), n = hi - lo;
     const int nchunk = (L + CH - 1) / CH;
-    float *qs = sm;                 // [G][QS]
+    float *qs = sm;                 // [hn][QS]; merge: weights
     float *ks = qs + G * QS;        // [CH][KS]   } merge: partial rows
     float *vs = ks + CH * KS;       // [CH][HD]   }
     float *sc = vs + CH * HD;       // [G][CH]
@@ -129,7 +155,7 @@ __device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const flo
     int *flag = reinterpret_cast<int *>(gred + (HD < 128 ? HD : 0));
     const bool has_new = pos >= lo && pos < hi;
     const int ncopy = has_new ? n - 1 : n;
-    const bool kwarp = has_new && warp == (G & 3);
+    const bool kwarp = has_new && warp == (hn & 3);
     const int half = r.rope_dim / 2;
     const int64_t lofs = (int64_t)layer * kv.layer_stride;
 
@@ -154,8 +180,8 @@ __device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const flo
             const int i = lane + 32 * j;
             cs[j] = i < half ? r.tab[(int64_t)pos * half + i] : make_float2(0.f, 0.f);
         }
-        for (int h = warp; h < G; h += 4) {
-            const float *src = a.q + (int64_t)t * qd + (int64_t)(g * G + h) * HD;
+        for (int h = warp; h < hn; h += 4) {
+            const float *src = a.q + (int64_t)t * qd + (int64_t)(g * G + h0 + h) * HD;
             float qv[PER];
 #pragma unroll
             for (int e = 0; e < PER; e++) qv[e] = __ldcg(src + lane + 32 * e);
@@ -172,11 +198,13 @@ __device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const flo
                 nk[e] = k_nw ? k_nw[lane + 32 * e] : 0.f;
             }
             norm_rope_regs<HD, NR>(kn, kx, k_nw != nullptr, nk, cs, half, r.interleaved, r.eps, lane);
-            float *kd = kv.k + lofs + newo, *vd = kv.v + lofs + newo;
+            if (h0 == 0) {  // one item of the group appends the new position
+                float *kd = kv.k + lofs + newo, *vd = kv.v + lofs + newo;
 #pragma unroll
-            for (int e = 0; e < PER; e++) {
-                kd[lane + 32 * e] = kn[lane + 32 * e];
-                vd[lane + 32 * e] = vn[lane + 32 * e];
+                for (int e = 0; e < PER; e++) {
+                    kd[lane + 32 * e] = kn[lane + 32 * e];
+                    vd[lane + 32 * e] = vn[lane + 32 * e];
+                }
             }
         }
     }
@@ -184,9 +212,9 @@ __device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const flo
     named_sync(bid, 128);
 
     // ---- scores (one lane per (head, position)) and the slice softmax ----
-    for (int b0 = warp * 32; b0 < G * CH; b0 += 128) {
+    for (int b0 = warp * 32; b0 < hn * CH; b0 += 128) {
         const int i = b0 + lane, h = i / CH, p = i - h * CH;
-        const bool ok = i < G * CH && p < n;
+        const bool ok = i < hn * CH && p < n;
         float s = -FLT_MAX;
         if (ok) {
             const float4 *qh = reinterpret_cast<const float4 *>(qs + h * QS);
@@ -209,7 +237,7 @@ __device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const flo
         float sum = e;
 #pragma unroll
         for (int o = CH / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (i < G * CH) {
+        if (i < hn * CH) {
             sc[h * CH + p] = nchunk == 1 ? __fdiv_rn(e, sum) : e;
             if (p == 0) {
                 stat[2 * h] = mx;
@@ -221,7 +249,7 @@ __device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const flo
 
     // ---- P.V, head by head; single chunk: the output, else the partial ----
     const int d = gtid % HD, gp = gtid / HD;
-    for (int h = 0; h < G; h++) {
+    for (int h = 0; h < hn; h++) {
         const float *sh = sc + h * CH;
         float acc = 0.f;
 #pragma unroll 4
@@ -234,9 +262,9 @@ __device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const flo
         }
         if (gp == 0) {
             if (nchunk == 1) {
-                a.out[(int64_t)t * qd + (int64_t)(g * G + h) * HD + d] = acc;
+                a.out[(int64_t)t * qd + (int64_t)(g * G + h0 + h) * HD + d] = acc;
             } else {
-                float *pp = a.part + (((int64_t)t * nh + g * G + h) * a.nsplit + c) * PS;
+                float *pp = a.part + (((int64_t)t * nh + g * G + h0 + h) * a.nsplit + c) * PS;
                 pp[d] = acc;
                 if (d == 0) {
                     pp[HD] = stat[2 * h];
@@ -250,11 +278,11 @@ __device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const flo
         return;
     }
 
-    // ---- arrival count; the last slice of (t, g) merges ----
+    // ---- arrival count; the last slice of (t, g, h0) merges ----
     __threadfence();
     named_sync(bid, 128);
     if (gtid == 0) {
-        int *cnt = a.counter + (int64_t)t * a.n_head_kv + g;
+        int *cnt = a.counter + (int64_t)t * nh + g * G + h0;
         const int old = atomicAdd(cnt, 1);
         const int last = old == nchunk - 1;
         if (last) *cnt = 0;  // ready for the next step
@@ -265,45 +293,45 @@ __device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const flo
         __threadfence();
         // merge buffer: the ks..vs region, CAP partial rows at a time
         float *buf = ks;
-        constexpr int CAP = (CH * KS + CH * HD) / PS;
-        if (G * nchunk <= CAP) {
-            // every head's partial rows in one round of copies
-            for (int h = 0; h < G; h++) {
-                const float *ph = a.part + ((int64_t)t * nh + g * G + h) * a.nsplit * PS;
-                float *bh = buf + h * nchunk * PS;
-                for (int i = gtid; i < nchunk * (PS / 4); i += 128) {
-                    const int cc = i / (PS / 4), piece = i - cc * (PS / 4);
-                    cp_async16(bh + cc * PS + piece * 4, ph + (int64_t)cc * PS + piece * 4);
-                }
+        constexpr int CAP = dec_merge_rows(HD, CH);
+        if (hn * nchunk <= CAP) {
+            // every head's partial rows in one round of copies (row hh * nchunk + cc)
+            for (int i = gtid; i < hn * nchunk * (PS / 4); i += 128) {
+                const int row = i / (PS / 4), piece = i - row * (PS / 4);
+                const int hh = row / nchunk, cc = row - hh * nchunk;
+                cp_async16(buf + row * PS + piece * 4,
+                           a.part + (((int64_t)t * nh + g * G + h0 + hh) * a.nsplit + cc) * PS + piece * 4);
             }
             cp_async_wait_all();
             named_sync(bid, 128);
-            for (int h = 0; h < G; h++) {
-                const float *bh = buf + h * nchunk * PS;
-                float M = -FLT_MAX, num = 0.f, den = 0.f;
-                for (int cc = 0; cc < nchunk; cc++) M = fmaxf(M, bh[cc * PS + HD]);
-                for (int cc = gp; cc < nchunk; cc += GROUPS) {
+            // per head (one warp each): maximum over the slices, their weights
+            // exp(m_c - M) and the softmax denominator sum_c w_c * (sum e)_c
+            float *wb = qs;  // [hn][nchunk]: hn * nchunk <= CAP <= QS
+            for (int hh = warp; hh < hn; hh += 4) {
+                const float *bh = buf + hh * nchunk * PS;
+                float M = -FLT_MAX;
+                for (int cc = lane; cc < nchunk; cc += 32) M = fmaxf(M, bh[cc * PS + HD]);
+                M = warp_max(M);
+                float den = 0.f;
+                for (int cc = lane; cc < nchunk; cc += 32) {
                     const float w = fast_exp(bh[cc * PS + HD] - M);
-                    num = fmaf(w, bh[cc * PS + d], num);
+                    wb[hh * nchunk + cc] = w;
                     den = fmaf(w, bh[cc * PS + HD + 1], den);
                 }
-                if (GROUPS > 1) {
-                    if (gp > 0) {
-                        gred[d] = num;
-                        if (d == 0) stat[0] = den;
-                    }
-                    named_sync(bid, 128);
-                    if (gp == 0) {
-                        num += gred[d];
-                        den += stat[0];
-                    }
-                    named_sync(bid, 128);
-                }
-                if (gp == 0) a.out[(int64_t)t * qd + (int64_t)(g * G + h) * HD + d] = num / den;
+                den = warp_sum(den);
+                if (lane == 0) stat[2 * hh + 1] = den;
+            }
+            named_sync(bid, 128);
+            for (int o = gtid; o < hn * HD; o += 128) {
+                const int hh = o / HD, dd = o - hh * HD;
+                const float *bh = buf + hh * nchunk * PS + dd, *wh = wb + hh * nchunk;
+                float num = 0.f;
+                for (int cc = 0; cc < nchunk; cc++) num = fmaf(wh[cc], bh[cc * PS], num);
+                a.out[(int64_t)t * qd + (int64_t)(g * G + h0 + hh) * HD + dd] = num / stat[2 * hh + 1];
             }
         } else
-        for (int h = 0; h < G; h++) {
-            const float *ph = a.part + ((int64_t)t * nh + g * G + h) * a.nsplit * PS;
+        for (int h = 0; h < hn; h++) {
+            const float *ph = a.part + ((int64_t)t * nh + g * G + h0 + h) * a.nsplit * PS;
             float M = -FLT_MAX, num = 0.f, den = 0.f;
             for (int c0 = 0; c0 < nchunk; c0 += CAP) {
                 const int nt = min(CAP, nchunk - c0);
@@ -341,7 +369,7 @@ __device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const flo
                 }
                 named_sync(bid, 128);
             }
-            if (gp == 0) a.out[(int64_t)t * qd + (int64_t)(g * G + h) * HD + d] = num / den;
+            if (gp == 0) a.out[(int64_t)t * qd + (int64_t)(g * G + h0 + h) * HD + d] = num / den;
         }
     }
     named_sync(bid, 128);

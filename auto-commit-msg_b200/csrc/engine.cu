@@ -472,7 +472,8 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
         RopeDesc rd{m->q, m->k, m->v, L.q_nw, L.k_nw, m->rope_tab, c.n_head, c.n_head_kv, hd, c.rope_dim,
                     c.rope_interleaved, eps};
         if (decode) {
-            AttnDesc ad{m->q, m->att, c.n_head, c.n_head_kv, hd, scale, m->part, m->dec_nsplit, m->d_attn_cnt};
+            AttnDesc ad{m->q, m->att, c.n_head, c.n_head_kv, hd, scale, m->part, m->dec_nsplit, m->d_attn_cnt,
+                        m->e->num_sms};
             CK_M(attention_decode_launch(rd, ad, kv, l, tm, ntok, max_pos, st));
         } else {
             CK_M(rope_append_launch(rd, kv, l, tm, ntok, st));
@@ -669,7 +670,7 @@ int mega_step(acm_model *m, bool greedy) {
     A.r = RopeDesc{m->q, m->k, m->v, nullptr, nullptr, m->rope_tab, c.n_head, c.n_head_kv, hd, c.rope_dim,
                    c.rope_interleaved, c.rms_eps};
     A.a = AttnDesc{m->q, m->att, c.n_head, c.n_head_kv, hd, 1.0f / (float)sqrt((double)hd), m->part,
-                   (c.max_ctx + DEC_CHUNK - 1) / DEC_CHUNK, m->d_attn_cnt};
+                   (c.max_ctx + DEC_CHUNK - 1) / DEC_CHUNK, m->d_attn_cnt, 0};
     A.kv = KVDesc{m->kpool, m->vpool, m->d_page_table, m->max_pages, PAGE, m->layer_stride, c.n_head_kv * hd};
     A.tm = TokMeta{m->d_seq, m->d_pos};
     A.bar = m->d_bar;
@@ -1146,8 +1147,8 @@ ACM_API int acm_model_finalize(acm_model *m) {
     const size_t part_rows = std::max<size_t>((size_t)PART_TOKSPLIT, (size_t)m->tdec * m->dec_nsplit);
     // rows of hd + 4 floats: the decode attention's partial stride (dec_part_stride)
     CK_M(dalloc(m, &m->part, part_rows * c.n_head * (hd + 4)));
-    CK_M(dalloc(m, &m->d_attn_cnt, (size_t)m->tdec * c.n_head_kv));
-    CK_M(cudaMemset(m->d_attn_cnt, 0, sizeof(int) * (size_t)m->tdec * c.n_head_kv));
+    CK_M(dalloc(m, &m->d_attn_cnt, (size_t)m->tdec * c.n_head));
+    CK_M(cudaMemset(m->d_attn_cnt, 0, sizeof(int) * (size_t)m->tdec * c.n_head));
     CK_M(dalloc(m, &m->logits, (size_t)m->max_seqs * c.vocab));
     CK_M(cudaMemset(m->logits, 0, sizeof(float) * (size_t)m->max_seqs * c.vocab));
     CK_M(dalloc(m, &m->d_tok, T));

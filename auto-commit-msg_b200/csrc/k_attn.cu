@@ -172,14 +172,19 @@ template <int HD>
 __global__ void __launch_bounds__(128) k_attn_decode(const RopeDesc r, const AttnDesc a, const KVDesc kv, int layer,
                                                      TokMeta tm) {
     extern __shared__ __align__(16) float sm[];
-    const int t = blockIdx.x, g = blockIdx.y, c = blockIdx.z;
+    const int G = a.n_head / a.n_head_kv;
+    const int t = blockIdx.x, g = blockIdx.y / G, j = blockIdx.y - g * G, c = blockIdx.z;
     if (threadIdx.x == 0) pdl_trigger();
     pdl_wait();
     const int seq = tm.seq[t], pos = tm.pos[t];
     if (c * ATT_CHUNK > pos) return;  // beyond this token's context
+    // head subset j of hn heads (chosen from this token's slice count)
+    const int hn = dec_heads_per_item(G, (pos + ATT_CHUNK) / ATT_CHUNK, a.n_head_kv, HD, ATT_CHUNK, a.min_items);
+    if ((j + 1) * hn > G) return;
     int64_t base, newo;
     dec_item_offsets(kv, seq, pos, g, c * ATT_CHUNK, HD, base, newo);
-    decode_attn_item<HD, ATT_CHUNK>(r, r.q_nw, r.k_nw, a, kv, layer, t, pos, g, c, base, newo, sm, threadIdx.x, 1);
+    decode_attn_item<HD, ATT_CHUNK>(r, r.q_nw, r.k_nw, a, kv, layer, t, pos, g, c, base, newo, sm, threadIdx.x, 1,
+                                    j * hn, hn);
 }
 
 cudaError_t attention_decode_launch(const RopeDesc &r, const AttnDesc &a, const KVDesc &kv, int layer, TokMeta tm,
@@ -192,7 +197,7 @@ cudaError_t attention_decode_launch(const RopeDesc &r, const AttnDesc &a, const 
     if (kv.page_size % ATT_CHUNK) return cudaErrorInvalidValue;
     const int HD = a.head_dim;
     const size_t smem = (size_t)dec_item_floats(HD, ATT_CHUNK, G) * sizeof(float);
-    dim3 grid(ntok, a.n_head_kv, nchunk);
+    dim3 grid(ntok, a.n_head, nchunk);  // y: kv head x head subset (unused subsets exit)
     cudaError_t e = HD == 128 ? launch_pdl(k_attn_decode<128>, grid, dim3(128), smem, st, r, a, kv, layer, tm)
                               : launch_pdl(k_attn_decode<64>, grid, dim3(128), smem, st, r, a, kv, layer, tm);
     if (e != cudaSuccess) return e;

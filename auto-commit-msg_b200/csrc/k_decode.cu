@@ -98,7 +98,7 @@ __device__ void attn_phase(const DecArgs &A, const DecPhase &P, float *area, Att
         for (int k = 0; k < mg.n; k++) {
             const AttnMeta m = mg.it[k];
             decode_attn_item<HD, DCH>(A.r, P.q_nw, P.k_nw, A.a, A.kv, P.layer, m.t, m.pos, m.g, m.c, m.base, m.newo,
-                                      sm, gtid, bid);
+                                      sm, gtid, bid, 0, A.a.n_head / nkv);
         }
         return;
     }
@@ -119,7 +119,8 @@ __device__ void attn_phase(const DecArgs &A, const DecPhase &P, float *area, Att
         int64_t base, newo;
         dec_item_offsets(A.kv, A.tm.seq[t], pos, g, c * DCH, HD, base, newo);
         if (k < DMETA && gtid == 0) mg.it[k] = AttnMeta{t, g, c, pos, base, newo};
-        decode_attn_item<HD, DCH>(A.r, P.q_nw, P.k_nw, A.a, A.kv, P.layer, t, pos, g, c, base, newo, sm, gtid, bid);
+        decode_attn_item<HD, DCH>(A.r, P.q_nw, P.k_nw, A.a, A.kv, P.layer, t, pos, g, c, base, newo, sm, gtid, bid, 0,
+                                  A.a.n_head / nkv);
     }
     if (P.layer == 0 && gtid == 0) mg.n = k;
 }

@@ -204,7 +204,8 @@ struct AttnDesc {
     float scale;
     float *part;      // split partials [ntok][n_head][nsplit][head_dim + 2]
     int nsplit;
-    int *counter;     // [ntok][n_head_kv] split-arrival counters (decode kernel)
+    int *counter;     // [ntok][n_head] split-arrival counters (decode kernel), one per item head subset
+    int min_items;    // decode kernel: smallest head subsets only while items < min_items (0: largest)
 };
 cudaError_t attention_launch(const AttnDesc &a, const KVDesc &kv, int layer, TokMeta tm, int ntok, int max_pos,
                              cudaStream_t st);

@@ -63,16 +63,27 @@ def allreduce(vals, world, op="max"):
     return t.tolist()
 
 
-def model_path(rank, world):
+# The model shapes of the parity workloads: (synth builder, file name, prompt
+# length, prompt seed, vocab).  qwen3 is the benchmark's own workload.
+MODELS = {
+    "qwen3": ("qwen3_06b", "qwen3-0.6b-q4km-seed0.gguf", PROMPT_LEN, 1, 151936),
+    "qwen2": ("qwen2_15b", "qwen2-1.5b-q8_0-seed0.gguf", 944, 3, 151936),
+    "llama_f16": ("llama32_1b_f16", "llama3.2-1b-f16-seed0.gguf", 1500, 4, 128256),
+    "llama_q5": ("llama32_1b_q5", "llama3.2-1b-q5-seed0.gguf", 1500, 4, 128256),
+}
+
+
+def model_path(rank, world, name="qwen3"):
     synth = importlib.import_module("auto-commit-msg_b200.synth")
-    path = os.path.join(MODEL_DIR, "qwen3-0.6b-q4km-seed0.gguf")
+    fn, fname, plen, pseed, vocab = MODELS[name]
+    path = os.path.join(MODEL_DIR, fname)
     if rank == 0 and not os.path.exists(path):
         os.makedirs(MODEL_DIR, exist_ok=True)
         tmp = path + f".tmp{os.getpid()}"
-        synth.build_model(synth.qwen3_06b(), tmp, seed=0)
+        synth.build_model(getattr(synth, fn)(), tmp, seed=0)
         os.replace(tmp, path)
     barrier(world)
-    return path, synth.prompt_ids(PROMPT_LEN, 151936, seed=1)
+    return path, synth.prompt_ids(plen, vocab, seed=pseed)
 
 
 def peaks():
@@ -460,7 +471,7 @@ def run_profile(args):
         print(f"gemv {args.type} {k}x{n}: {sec * 1e6:.2f} us, {w.size / sec / 1e9:.1f} GB/s", flush=True)
         eng.close()
         return
-    path, prompt = model_path(0, 1)
+    path, prompt = model_path(0, 1, args.model)
     eng = acm.Engine(0)
     if args.profile == "load":
         for i in range(3):  # GGUF parse + upload of every tensor + finalize, wall clock
@@ -517,6 +528,8 @@ def main():
                     help="run a short workload for the profiler instead of the benchmark")
     ap.add_argument("--tokens", type=int, default=8, help="decode tokens of --profile decode/trace")
     ap.add_argument("--type", choices=list(KB_TYPES), default="q4_k", help="weight type of --profile gemv")
+    ap.add_argument("--model", choices=list(MODELS), default="qwen3",
+                    help="model shape of --profile prefill/decode/trace/load (qwen3: the benchmark's own)")
     ap.add_argument("--workload", choices=["single", "serve", "kernels"], default="single",
                     help="single: the batch-1 Generate benchmark (default); serve: 512 requests through acm_serve; "
                          "kernels: the matmul microbench over every quantized type and weight shape")
