@@ -205,16 +205,15 @@ static cudaError_t gemv_launch_group(const GemvSegDesc *segs, int nseg, int ta, 
     const size_t xb = x_bytes(k, mt, a.lpr);
     // a stage holds R rows plus up to 60 bytes of 16-byte rounding (two
     // copies) and the 4-byte over-read of the unaligned word loader
-    int64_t sb = std::max<int64_t>(32 * 1024, ((maxrow + 64 + 127) / 128) * 128);
-    if (a.lpr) {
-        // enough rows per stage for every consumer warp to take a row group
-        const int ncw = mt <= 2 ? 16 : 8;
-        sb = std::max<int64_t>(sb, (((int64_t)ncw * (32 / a.lpr) * maxrow + 64 + 127) / 128) * 128);
-    }
+    // enough rows per stage for every consumer warp to take a row (wide
+    // path: a row group)
+    const int ncw = mt <= 2 ? 16 : 8;
+    int64_t sb = std::max<int64_t>(32 * 1024, (((int64_t)ncw * maxrow + 64 + 127) / 128) * 128);
+    if (a.lpr) sb = std::max<int64_t>(sb, (((int64_t)ncw * (32 / a.lpr) * maxrow + 64 + 127) / 128) * 128);
     int ns = (int)std::min<int64_t>(6, ((int64_t)SMEM_MAX - (int64_t)xb - 16) / sb);
-    if (ns < 2 && a.lpr) {
-        // long rows (Q8_0 / F16 at K >= 1024): two stages as large as shared
-        // memory allows; the stage then feeds fewer warps, but the ring stays
+    if (ns < 2) {
+        // long rows (F16 / Q8_0 at large K): two stages as large as shared
+        // memory allows; a stage then feeds fewer warps, but the ring stays
         // double-buffered (one-row stages serialise the copies row by row)
         sb = (((int64_t)SMEM_MAX - (int64_t)xb - 16) / 2) & ~int64_t(127);
         ns = 2;
