@@ -80,7 +80,7 @@ __device__ __forceinline__ bool grid_sync(unsigned *bar, unsigned target, int *a
 // enumerates them and caches their cache offsets in shared memory.
 constexpr int DMETA = 4;  // cached items per group
 struct AttnMeta {
-    int t, g, c, pos;
+    int t, g, c, pos, h0, hn;
     int64_t base, newo;
 };
 struct AttnMetaGroup {
@@ -98,29 +98,36 @@ __device__ void attn_phase(const DecArgs &A, const DecPhase &P, float *area, Att
         for (int k = 0; k < mg.n; k++) {
             const AttnMeta m = mg.it[k];
             decode_attn_item<HD, DCH>(A.r, P.q_nw, P.k_nw, A.a, A.kv, P.layer, m.t, m.pos, m.g, m.c, m.base, m.newo,
-                                      sm, gtid, bid, 0, A.a.n_head / nkv);
+                                      sm, gtid, bid, m.h0, m.hn);
         }
         return;
     }
-    // items enumerated token by token: (t, g, c) with c < ceil(L_t / DCH)
+    // items enumerated token by token: (t, g, j, c) with c < ceil(L_t / DCH)
+    // and j a subset of hn_t query heads of kv head g
+    const int G = A.a.n_head / nkv, slots = (int)gridDim.x * DGROUPS;
     int total = 0;
-    for (int t = 0; t < A.ntok; t++) total += nkv * ((A.tm.pos[t] + DCH) / DCH);
+    for (int t = 0; t < A.ntok; t++) {
+        const int nch = (A.tm.pos[t] + DCH) / DCH;
+        total += nkv * (G / dec_heads_per_item(G, nch, nkv, HD, DCH, slots)) * nch;
+    }
     int k = 0;
     for (int item = blockIdx.x * DGROUPS + grp; item < total; item += gridDim.x * DGROUPS, k++) {
-        int t = 0, rem = item;
+        int t = 0, rem = item, nch = 0, hn = 1;
         while (true) {
-            const int cnt = nkv * ((A.tm.pos[t] + DCH) / DCH);
+            nch = (A.tm.pos[t] + DCH) / DCH;
+            hn = dec_heads_per_item(G, nch, nkv, HD, DCH, slots);
+            const int cnt = nkv * (G / hn) * nch;
             if (rem < cnt) break;
             rem -= cnt;
             t++;
         }
-        const int pos = A.tm.pos[t], nch = (pos + DCH) / DCH;
-        const int g = rem / nch, c = rem % nch;
+        const int pos = A.tm.pos[t];
+        const int gj = rem / nch, c = rem % nch, g = gj / (G / hn), h0 = (gj % (G / hn)) * hn;
         int64_t base, newo;
         dec_item_offsets(A.kv, A.tm.seq[t], pos, g, c * DCH, HD, base, newo);
-        if (k < DMETA && gtid == 0) mg.it[k] = AttnMeta{t, g, c, pos, base, newo};
-        decode_attn_item<HD, DCH>(A.r, P.q_nw, P.k_nw, A.a, A.kv, P.layer, t, pos, g, c, base, newo, sm, gtid, bid, 0,
-                                  A.a.n_head / nkv);
+        if (k < DMETA && gtid == 0) mg.it[k] = AttnMeta{t, g, c, pos, h0, hn, base, newo};
+        decode_attn_item<HD, DCH>(A.r, P.q_nw, P.k_nw, A.a, A.kv, P.layer, t, pos, g, c, base, newo, sm, gtid, bid,
+                                  h0, hn);
     }
     if (P.layer == 0 && gtid == 0) mg.n = k;
 }

@@ -171,6 +171,32 @@ static cudaError_t launch_types(GemvArgs &a, int ta, int tb, int grid, size_t sm
     return cudaErrorInvalidValue;
 }
 
+// CTAs per segment in proportion to its bytes, at least one and at most one
+// per row, summing to at most num_sms (largest remainders get the rounding),
+// so that a launch of one CTA per SM never spills into a second wave.
+static void split_ctas(const GemvSegDesc *segs, int nseg, int64_t k, int num_sms, int *nc) {
+    double total = 0, want[GEMV_MAX_SEG];
+    for (int i = 0; i < nseg; i++) total += (double)row_bytes(segs[i].type, k) * (segs[i].w2 ? 2 : 1) * segs[i].n;
+    int used = 0;
+    for (int i = 0; i < nseg; i++) {
+        want[i] = (double)row_bytes(segs[i].type, k) * (segs[i].w2 ? 2 : 1) * segs[i].n / total * num_sms;
+        nc[i] = std::max(1, std::min<int>((int)want[i], (int)segs[i].n));
+        used += nc[i];
+    }
+    while (used < num_sms) {
+        int best = -1;
+        double rem = -1.0;
+        for (int i = 0; i < nseg; i++)
+            if (nc[i] < segs[i].n && want[i] - nc[i] > rem) {
+                rem = want[i] - nc[i];
+                best = i;
+            }
+        if (best < 0 || rem <= 0.0) break;
+        nc[best]++;
+        used++;
+    }
+}
+
 // One launch for segments whose types are {ta} or {ta, tb}.
 static cudaError_t gemv_launch_group(const GemvSegDesc *segs, int nseg, int ta, int tb, const float *x, int ldx,
                                      int64_t k, int m, const float *norm_w, float eps, int num_sms, cudaStream_t st,
@@ -188,12 +214,7 @@ static cudaError_t gemv_launch_group(const GemvSegDesc *segs, int nseg, int ta, 
     a.norm_w = norm_w;
     a.eps = eps;
     int64_t maxrow = 0;
-    double total_bytes = 0;
-    for (int i = 0; i < nseg; i++) {
-        const int64_t rb = row_bytes(segs[i].type, k) * (segs[i].w2 ? 2 : 1);
-        maxrow = std::max(maxrow, rb);
-        total_bytes += (double)rb * (double)segs[i].n;
-    }
+    for (int i = 0; i < nseg; i++) maxrow = std::max(maxrow, row_bytes(segs[i].type, k) * (segs[i].w2 ? 2 : 1));
     // wide path: a single large matrix whose format has a span decoder
     a.lpr = 0;
     if (nseg == 1 && sb_ok(segs[0].type) && k % 256 == 0 && segs[0].n / num_sms >= 128) {
@@ -226,12 +247,13 @@ static cudaError_t gemv_launch_group(const GemvSegDesc *segs, int nseg, int ta, 
     // small matrices: shrink the ring to the stages a CTA actually needs, so
     // the kernel's shared memory leaves room for the next kernel's CTAs to
     // start early (programmatic dependent launch) and prefetch their weights
+    int ncta[GEMV_MAX_SEG];
+    split_ctas(segs, nseg, k, num_sms, ncta);
     {
         int64_t need_stages = 1, need_bytes = 0;
         for (int i = 0; i < nseg; i++) {
             const int64_t rbp = row_bytes(segs[i].type, k) * (segs[i].w2 ? 2 : 1);
-            const double share = (double)rbp * (double)segs[i].n / total_bytes;
-            const int nc = std::max(1, std::min<int>((int)(share * num_sms + 0.5), (int)segs[i].n));
+            const int nc = ncta[i];
             const int64_t rows = (segs[i].n + nc - 1) / nc;
             const int64_t rps = (sb - 64) / rbp;
             need_stages = std::max<int64_t>(need_stages, (rows + rps - 1) / std::max<int64_t>(rps, 1));
@@ -263,9 +285,7 @@ static cudaError_t gemv_launch_group(const GemvSegDesc *segs, int nseg, int ta, 
         g.bias = d.bias;
         g.yrow = d.yrow;
         g.amax = d.amax;
-        const double share = (double)(g.rb + g.rb2) * (double)d.n / total_bytes;
-        int nc = (int)(share * num_sms + 0.5);
-        nc = std::max(1, std::min<int>(nc, (int)d.n));
+        const int nc = ncta[i];
         g.ncta = nc;
         g.cta0 = grid;
         grid += nc;
