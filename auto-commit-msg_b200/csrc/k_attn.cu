@@ -172,14 +172,17 @@ template <int HD>
 __global__ void __launch_bounds__(128) k_attn_decode(const RopeDesc r, const AttnDesc a, const KVDesc kv, int layer,
                                                      TokMeta tm) {
     extern __shared__ __align__(16) float sm[];
-    const int G = a.n_head / a.n_head_kv;
-    const int t = blockIdx.x, g = blockIdx.y / G, j = blockIdx.y - g * G, c = blockIdx.z;
+    const int G = a.n_head / a.n_head_kv, nsub = (int)gridDim.y / a.n_head_kv;  // nsub: 1 or G
+    const int t = blockIdx.x, g = blockIdx.y / nsub, j = blockIdx.y - g * nsub, c = blockIdx.z;
     if (threadIdx.x == 0) pdl_trigger();
     pdl_wait();
     const int seq = tm.seq[t], pos = tm.pos[t];
     if (c * ATT_CHUNK > pos) return;  // beyond this token's context
-    // head subset j of hn heads (chosen from this token's slice count)
-    const int hn = dec_heads_per_item(G, (pos + ATT_CHUNK) / ATT_CHUNK, a.n_head_kv, HD, ATT_CHUNK, a.min_items);
+    // head subset j of hn heads (chosen from this token's slice count; the
+    // launch's tokens share the item target); one subset when the launch has
+    // no room for more
+    const int mi = (a.min_items + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int hn = nsub == 1 ? G : dec_heads_per_item(G, (pos + ATT_CHUNK) / ATT_CHUNK, a.n_head_kv, HD, ATT_CHUNK, mi);
     if ((j + 1) * hn > G) return;
     int64_t base, newo;
     dec_item_offsets(kv, seq, pos, g, c * ATT_CHUNK, HD, base, newo);
@@ -197,7 +200,11 @@ cudaError_t attention_decode_launch(const RopeDesc &r, const AttnDesc &a, const 
     if (kv.page_size % ATT_CHUNK) return cudaErrorInvalidValue;
     const int HD = a.head_dim;
     const size_t smem = (size_t)dec_item_floats(HD, ATT_CHUNK, G) * sizeof(float);
-    dim3 grid(ntok, a.n_head, nchunk);  // y: kv head x head subset (unused subsets exit)
+    // y: kv head x head subset (unused subsets exit).  Query heads are split
+    // over items only while the launch has few (token, kv head) pairs: with
+    // many tokens the extra CTAs would mostly exit at once.
+    const int nsub = (int64_t)ntok * a.n_head_kv * 4 >= (a.min_items > 1 ? a.min_items : 1) ? 1 : G;
+    dim3 grid(ntok, a.n_head_kv * nsub, nchunk);
     cudaError_t e = HD == 128 ? launch_pdl(k_attn_decode<128>, grid, dim3(128), smem, st, r, a, kv, layer, tm)
                               : launch_pdl(k_attn_decode<64>, grid, dim3(128), smem, st, r, a, kv, layer, tm);
     if (e != cudaSuccess) return e;
