@@ -84,6 +84,7 @@ SIGNATURES = {
     "acm_sample_dev_noalloc": (C.c_int, [P, P, C.c_int64, C.c_int32, C.c_int32, P, P, P]),
     "acm_engine_stream": (P, [P]),
     "acm_engine_sync": (C.c_int, [P]),
+    "acm_engine_set_kv_f16": (C.c_int, [P, C.c_int32]),
     "acm_model_last_timing": (C.c_int, [P, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "acm_kernel_launches": (C.c_uint64, []),
     "acm_model_bench_gemm": (C.c_int, [P, C.c_int32, C.c_int32, C.POINTER(C.c_double), C.POINTER(C.c_double),

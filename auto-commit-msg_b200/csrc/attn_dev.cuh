@@ -10,6 +10,16 @@
 
 namespace acm {
 
+// One cache element at element offset `off` of a pool (fp32, or IEEE half
+// for the reduced-precision cache: round to nearest even on store).
+__device__ __forceinline__ void kv_store(float *pool, int64_t off, float v, bool f16) {
+    if (f16) reinterpret_cast<__half *>(pool)[off] = __float2half_rn(v);
+    else pool[off] = v;
+}
+__device__ __forceinline__ float kv_load(const float *pool, int64_t off, bool f16) {
+    return f16 ? __half2float(reinterpret_cast<const __half *>(pool)[off]) : pool[off];
+}
+
 __device__ __forceinline__ const float *kv_row(const float *pool, const KVDesc &kv, int layer, int seq, int pos) {
     const int page = kv.page_table[(int64_t)seq * kv.max_pages + (pos / kv.page_size)];
     return pool + (int64_t)layer * kv.layer_stride + ((int64_t)page * kv.page_size + (pos % kv.page_size)) * kv.kvd;
@@ -134,8 +144,11 @@ __device__ __forceinline__ void dec_item_offsets(const KVDesc &kv, int seq, int 
 // slices fits dec_merge_rows, else per head in tiles); per-head maxima and
 // weights are warp reductions, the outputs one (head, dim) per thread.
 // Register use stays small so the item also runs inside the persistent
-// decode kernel's 96-register budget.
-template <int HD, int CH>
+// decode kernel's 96-register budget.  KH: the cache holds IEEE half (the
+// reduced-precision cache); its rows are loaded into registers first,
+// widened into the same fp32 staging rows once the query heads are ready,
+// and the appended key/value are rounded to half before they are used.
+template <int HD, int CH, bool KH = false>
 __device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const float *k_nw, const AttnDesc &a,
                                  const KVDesc &kv, int layer, int t, int pos, int g, int c, int64_t base,
                                  int64_t newo, float *sm, int gtid, int bid, int h0, int hn) {
@@ -160,13 +173,27 @@ __device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const flo
     const int64_t lofs = (int64_t)layer * kv.layer_stride;
 
     // ---- cached rows of the slice: asynchronous copies, all in flight ----
-    {
+    constexpr int CPH = HD / 8;                    // 16-byte pieces per fp16 row
+    constexpr int NPH = KH ? (CH * CPH + 127) / 128 : 1;
+    uint4 kreg[NPH], vreg[NPH];
+    if constexpr (!KH) {
         constexpr int CPR = HD / 4;  // 16-byte pieces per row
         const float *kb = kv.k + lofs + base, *vb = kv.v + lofs + base;
         for (int i = gtid; i < ncopy * CPR; i += 128) {  // K and V piece together, constant divisors
             const int p = i / CPR, piece = i - p * CPR;
             cp_async16(ks + p * KS + piece * 4, kb + (int64_t)p * kv.kvd + piece * 4);
             cp_async16(vs + p * HD + piece * 4, vb + (int64_t)p * kv.kvd + piece * 4);
+        }
+    } else {
+        const __half *kb = reinterpret_cast<const __half *>(kv.k) + lofs + base;
+        const __half *vb = reinterpret_cast<const __half *>(kv.v) + lofs + base;
+#pragma unroll
+        for (int j = 0; j < NPH; j++) {
+            const int i = gtid + 128 * j, p = i / CPH, piece = i - p * CPH;
+            if (i < ncopy * CPH) {
+                kreg[j] = __ldg(reinterpret_cast<const uint4 *>(kb + (int64_t)p * kv.kvd + piece * 8));
+                vreg[j] = __ldg(reinterpret_cast<const uint4 *>(vb + (int64_t)p * kv.kvd + piece * 8));
+            }
         }
     }
     // ---- query heads (and the new key): loads, then norm + rope ----
@@ -198,12 +225,39 @@ __device__ void decode_attn_item(const RopeDesc &r, const float *q_nw, const flo
                 nk[e] = k_nw ? k_nw[lane + 32 * e] : 0.f;
             }
             norm_rope_regs<HD, NR>(kn, kx, k_nw != nullptr, nk, cs, half, r.interleaved, r.eps, lane);
-            if (h0 == 0) {  // one item of the group appends the new position
-                float *kd = kv.k + lofs + newo, *vd = kv.v + lofs + newo;
+            if constexpr (KH) {  // the values later steps will read back
 #pragma unroll
                 for (int e = 0; e < PER; e++) {
-                    kd[lane + 32 * e] = kn[lane + 32 * e];
-                    vd[lane + 32 * e] = vn[lane + 32 * e];
+                    kn[lane + 32 * e] = __half2float(__float2half_rn(kn[lane + 32 * e]));
+                    vn[lane + 32 * e] = __half2float(__float2half_rn(vn[lane + 32 * e]));
+                }
+            }
+            if (h0 == 0) {  // one item of the group appends the new position
+#pragma unroll
+                for (int e = 0; e < PER; e++) {
+                    kv_store(kv.k, lofs + newo + lane + 32 * e, kn[lane + 32 * e], KH);
+                    kv_store(kv.v, lofs + newo + lane + 32 * e, vn[lane + 32 * e], KH);
+                }
+            }
+        }
+    }
+    if constexpr (KH) {  // widen the fp16 rows into the staging rows
+#pragma unroll
+        for (int j = 0; j < NPH; j++) {
+            const int i = gtid + 128 * j, p = i / CPH, piece = i - p * CPH;
+            if (i < ncopy * CPH) {
+                const uint32_t kw[4] = {kreg[j].x, kreg[j].y, kreg[j].z, kreg[j].w};
+                const uint32_t vw[4] = {vreg[j].x, vreg[j].y, vreg[j].z, vreg[j].w};
+                float4 *kd = reinterpret_cast<float4 *>(ks + p * KS + piece * 8);
+                float4 *vd = reinterpret_cast<float4 *>(vs + p * HD + piece * 8);
+#pragma unroll
+                for (int w = 0; w < 2; w++) {
+                    const float2 k0 = __half22float2(*reinterpret_cast<const __half2 *>(&kw[2 * w]));
+                    const float2 k1 = __half22float2(*reinterpret_cast<const __half2 *>(&kw[2 * w + 1]));
+                    const float2 v0 = __half22float2(*reinterpret_cast<const __half2 *>(&vw[2 * w]));
+                    const float2 v1 = __half22float2(*reinterpret_cast<const __half2 *>(&vw[2 * w + 1]));
+                    kd[w] = make_float4(k0.x, k0.y, k1.x, k1.y);
+                    vd[w] = make_float4(v0.x, v0.y, v1.x, v1.y);
                 }
             }
         }

@@ -66,6 +66,7 @@ struct acm_engine {
     size_t scratch_bytes = 0;
     void *scratch2 = nullptr;  // operand splits of acm_matmul_dev's tensor-core path
     size_t scratch2_bytes = 0;
+    int kv_f16 = 0;            // KV cache type of models created from now on (1: IEEE half)
 };
 
 namespace {
@@ -131,8 +132,9 @@ struct acm_model {
 
     // paged KV cache
     int max_pages = 0, n_pages = 0;
-    float *kpool = nullptr, *vpool = nullptr;
-    int64_t layer_stride = 0;
+    float *kpool = nullptr, *vpool = nullptr;  // fp32, or IEEE half elements when kv_f16
+    int64_t layer_stride = 0;                  // elements
+    int kv_f16 = 0;
     std::vector<int> free_pages;
     int32_t *d_page_table = nullptr;
     Pinned<int32_t> h_page_table;
@@ -370,6 +372,7 @@ int attention_prefill_mma(acm_model *m, int layer, int seq, int pos0, int ntok) 
     o.q = m->q;
     o.kc = m->kpool;
     o.vc = m->vpool;
+    o.kv_f16 = m->kv_f16;
     o.page_row = m->d_page_table + (int64_t)seq * m->max_pages;
     o.layer_off = (int64_t)layer * m->layer_stride;
     o.page_size = PAGE;
@@ -437,7 +440,7 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
     const int S = m->e->num_sms;
     const float eps = c.rms_eps;
     CK_M(dequant_launch(m->embd->type, m->embd->d, E, ntok, m->d_tok, m->embd->rows(), m->x, E, st));
-    KVDesc kv{m->kpool, m->vpool, m->d_page_table, m->max_pages, PAGE, m->layer_stride, kvd};
+    KVDesc kv{m->kpool, m->vpool, m->d_page_table, m->max_pages, PAGE, m->layer_stride, kvd, m->kv_f16};
     TokMeta tm{m->d_seq, m->d_pos};
     const float scale = 1.0f / (float)sqrt((double)hd);
     const int nsplit = attn_nsplit(m, ntok, max_pos);
@@ -614,7 +617,7 @@ bool mega_enabled() {
 bool mega_ready(acm_model *m) {
     if (m->dplan_state) return m->dplan_state > 0;
     m->dplan_state = -1;
-    if (!mega_enabled()) return false;
+    if (!mega_enabled() || m->kv_f16) return false;  // the persistent kernel reads an fp32 cache
     const acm_config &c = m->c;
     std::vector<DecLayerDesc> Ls(c.n_layers);
     for (int l = 0; l < c.n_layers; l++) {
@@ -671,7 +674,7 @@ int mega_step(acm_model *m, bool greedy) {
                    c.rope_interleaved, c.rms_eps};
     A.a = AttnDesc{m->q, m->att, c.n_head, c.n_head_kv, hd, 1.0f / (float)sqrt((double)hd), m->part,
                    (c.max_ctx + DEC_CHUNK - 1) / DEC_CHUNK, m->d_attn_cnt, 0};
-    A.kv = KVDesc{m->kpool, m->vpool, m->d_page_table, m->max_pages, PAGE, m->layer_stride, c.n_head_kv * hd};
+    A.kv = KVDesc{m->kpool, m->vpool, m->d_page_table, m->max_pages, PAGE, m->layer_stride, c.n_head_kv * hd, 0};
     A.tm = TokMeta{m->d_seq, m->d_pos};
     A.bar = m->d_bar;
     A.tok = m->d_tok;
@@ -876,6 +879,12 @@ ACM_API int acm_engine_sync(acm_engine *e) {
     return ACM_OK;
 }
 
+ACM_API int acm_engine_set_kv_f16(acm_engine *e, int32_t enable) {
+    if (!e) return ACM_ERR_INVALID;
+    e->kv_f16 = enable ? 1 : 0;
+    return ACM_OK;
+}
+
 ACM_API int acm_model_create(acm_engine *e, const acm_config *cfg, int32_t max_seqs, acm_model **out) {
     if (!e || !cfg || !out || max_seqs < 1 || max_seqs > 1024) return ACM_ERR_INVALID;
     *out = nullptr;
@@ -889,6 +898,7 @@ ACM_API int acm_model_create(acm_engine *e, const acm_config *cfg, int32_t max_s
     e->models++;
     m->c = c;
     m->max_seqs = max_seqs;
+    m->kv_f16 = e->kv_f16;
     *out = m;
     return ACM_OK;
 }
@@ -1122,8 +1132,10 @@ ACM_API int acm_model_finalize(acm_model *m) {
     m->max_pages = (c.max_ctx + PAGE - 1) / PAGE;
     m->n_pages = m->max_pages * m->max_seqs;
     m->layer_stride = (int64_t)m->n_pages * PAGE * kvd;
-    CK_M(dalloc(m, &m->kpool, (size_t)m->layer_stride * c.n_layers));
-    CK_M(dalloc(m, &m->vpool, (size_t)m->layer_stride * c.n_layers));
+    const size_t pool_floats = m->kv_f16 ? ((size_t)m->layer_stride * c.n_layers + 1) / 2
+                                         : (size_t)m->layer_stride * c.n_layers;
+    CK_M(dalloc(m, &m->kpool, pool_floats));
+    CK_M(dalloc(m, &m->vpool, pool_floats));
     m->free_pages.clear();
     for (int p = m->n_pages - 1; p >= 0; p--) m->free_pages.push_back(p);
     CK_M(dalloc(m, &m->d_page_table, (size_t)m->max_seqs * m->max_pages));

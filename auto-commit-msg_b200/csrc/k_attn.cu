@@ -186,8 +186,12 @@ __global__ void __launch_bounds__(128) k_attn_decode(const RopeDesc r, const Att
     if ((j + 1) * hn > G) return;
     int64_t base, newo;
     dec_item_offsets(kv, seq, pos, g, c * ATT_CHUNK, HD, base, newo);
-    decode_attn_item<HD, ATT_CHUNK>(r, r.q_nw, r.k_nw, a, kv, layer, t, pos, g, c, base, newo, sm, threadIdx.x, 1,
-                                    j * hn, hn);
+    if (kv.f16)
+        decode_attn_item<HD, ATT_CHUNK, true>(r, r.q_nw, r.k_nw, a, kv, layer, t, pos, g, c, base, newo, sm,
+                                              threadIdx.x, 1, j * hn, hn);
+    else
+        decode_attn_item<HD, ATT_CHUNK, false>(r, r.q_nw, r.k_nw, a, kv, layer, t, pos, g, c, base, newo, sm,
+                                               threadIdx.x, 1, j * hn, hn);
 }
 
 cudaError_t attention_decode_launch(const RopeDesc &r, const AttnDesc &a, const KVDesc &kv, int layer, TokMeta tm,
@@ -269,11 +273,25 @@ __global__ void __launch_bounds__(256) k_attn_prefill(const AttnDesc a, const KV
                                  ((int64_t)kv.page_table[(int64_t)seq * kv.max_pages + k0 / kv.page_size] * kv.page_size +
                                   (k0 % kv.page_size)) * kv.kvd + g * HD;
             const int pieces = kn * (HD / 4);
-            for (int i = tid; i < pieces * (pass + 1); i += 256) {
-                const int which = i / pieces, rem = i - which * pieces;
-                const int p = rem / (HD / 4), c = rem - p * (HD / 4);
-                const float *src = (which ? kv.v : kv.k) + base + (int64_t)p * kv.kvd + c * 4;
-                cp_async16(which ? vs + p * HD + c * 4 : ks + p * QS + c * 4, src);
+            if (kv.f16) {  // fp16 cache: 4 halves per piece, widened on the way in
+                for (int i = tid; i < pieces * (pass + 1); i += 256) {
+                    const int which = i / pieces, rem = i - which * pieces;
+                    const int p = rem / (HD / 4), c = rem - p * (HD / 4);
+                    const __half *src = reinterpret_cast<const __half *>(which ? kv.v : kv.k) + base +
+                                        (int64_t)p * kv.kvd + c * 4;
+                    const uint2 hv = *reinterpret_cast<const uint2 *>(src);
+                    const float2 a0 = __half22float2(*reinterpret_cast<const __half2 *>(&hv.x));
+                    const float2 a1 = __half22float2(*reinterpret_cast<const __half2 *>(&hv.y));
+                    *reinterpret_cast<float4 *>(which ? vs + p * HD + c * 4 : ks + p * QS + c * 4) =
+                        make_float4(a0.x, a0.y, a1.x, a1.y);
+                }
+            } else {
+                for (int i = tid; i < pieces * (pass + 1); i += 256) {
+                    const int which = i / pieces, rem = i - which * pieces;
+                    const int p = rem / (HD / 4), c = rem - p * (HD / 4);
+                    const float *src = (which ? kv.v : kv.k) + base + (int64_t)p * kv.kvd + c * 4;
+                    cp_async16(which ? vs + p * HD + c * 4 : ks + p * QS + c * 4, src);
+                }
             }
             cp_async_wait_all();
             __syncthreads();
@@ -393,7 +411,7 @@ cudaError_t attention_launch(const AttnDesc &a, const KVDesc &kv, int layer, Tok
                              cudaStream_t st) {
     if (ntok <= 0) return cudaSuccess;
     const int G = a.n_head / a.n_head_kv;
-    if (G > 8 || a.n_head % a.n_head_kv) return cudaErrorInvalidValue;
+    if (G > 8 || a.n_head % a.n_head_kv || kv.f16) return cudaErrorInvalidValue;  // fp32 cache only
     const int L = max_pos + 1;
     const int chunk_max = (L + a.nsplit - 1) / a.nsplit;
     const int HD = a.head_dim;

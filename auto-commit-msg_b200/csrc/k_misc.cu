@@ -8,6 +8,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "launch.cuh"
+#include "attn_dev.cuh"
 #include "quant.cuh"
 
 namespace acm {
@@ -146,8 +147,8 @@ __global__ void __launch_bounds__(256) k_rope_append(const RopeDesc r, const KVD
         const int64_t off = kv_off(kv, layer, seq, pos) + (int64_t)g * hd;
         const float *vs = r.v + (int64_t)t * kvd + g * hd;
         for (int d = lane; d < hd; d += 32) {
-            kv.k[off + d] = vec[d];
-            kv.v[off + d] = vs[d];
+            kv_store(kv.k, off + d, vec[d], kv.f16);
+            kv_store(kv.v, off + d, vs[d], kv.f16);
         }
     }
 }

@@ -401,7 +401,8 @@ __global__ void k_split_weight(const uint8_t *w, int64_t n, int k, __nv_bfloat16
 // ---------------------------------------------------------------------------
 struct AttnSplitArgs {
     const float *q;             // [ntok][nh*HD] (normed + roped)
-    const float *kc, *vc;       // cache pools
+    const float *kc, *vc;       // cache pools (fp16 elements when kv_f16)
+    int kv_f16;
     const int32_t *page_row;    // page table row of the sequence
     int64_t layer_off;          // floats
     int page_size, kvd;
@@ -427,8 +428,9 @@ __global__ void __launch_bounds__(256) k_attn_split(const AttnSplitArgs a) {
         for (int i = tid; i < 64 * hd; i += 256) {
             const int pr = i / hd, d = i - pr * hd, p = p0 + pr;
             const bool ok = p < a.L;
-            const float kv = ok ? a.kc[rowbase + (int64_t)pr * a.kvd + d] : 0.f;
-            const float vv = ok ? a.vc[rowbase + (int64_t)pr * a.kvd + d] : 0.f;
+            const int64_t e = rowbase + (int64_t)pr * a.kvd + d;
+            const float kv = ok ? (a.kv_f16 ? __half2float(reinterpret_cast<const __half *>(a.kc)[e]) : a.kc[e]) : 0.f;
+            const float vv = ok ? (a.kv_f16 ? __half2float(reinterpret_cast<const __half *>(a.vc)[e]) : a.vc[e]) : 0.f;
             __nv_bfloat16 h, l;
             split_bf16(kv, h, l);
             const int64_t ek = kbase + blk64(p, d, hd);
@@ -577,7 +579,7 @@ cudaError_t split_weight_launch(int type, const void *w, int64_t n, int k, void 
 
 cudaError_t attn_split_launch(const AttnMmaOps &o, cudaStream_t st) {
     if (o.hd > 128 || o.hd % 64 || o.page_size % 64 || o.Lp % 64) return cudaErrorInvalidValue;
-    AttnSplitArgs a{o.q,  o.kc, o.vc, o.page_row, o.layer_off, o.page_size, o.kvd, o.ntok, o.L,  o.Lp, o.G,
+    AttnSplitArgs a{o.q,  o.kc, o.vc, o.kv_f16, o.page_row, o.layer_off, o.page_size, o.kvd, o.ntok, o.L,  o.Lp, o.G,
                     o.nh, o.hd, o.rq, static_cast<__nv_bfloat16 *>(o.qh), static_cast<__nv_bfloat16 *>(o.ql),
                     static_cast<__nv_bfloat16 *>(o.kh), static_cast<__nv_bfloat16 *>(o.kl),
                     static_cast<__nv_bfloat16 *>(o.vh), static_cast<__nv_bfloat16 *>(o.vl)};

@@ -146,7 +146,8 @@ cudaError_t mma_gemm_batched_launch(const MmaGemmSeg *segs, int nseg, const Tens
 // Prefill attention on the tensor cores: operand preparation (k_attn_split)
 // and the softmax between S = Q.K^T and O = P.V (k_attn_softmax).
 struct AttnMmaOps {
-    const float *q, *kc, *vc;
+    const float *q, *kc, *vc;  // kc, vc: fp16 elements when kv_f16
+    int kv_f16;
     const int32_t *page_row;
     int64_t layer_off;
     int page_size, kvd, ntok, L, Lp, G, nh, hd, nkv, pos0;
@@ -175,12 +176,13 @@ struct TokMeta {
 
 // Paged KV cache geometry.
 struct KVDesc {
-    float *k, *v;               // pools [layer][page][page_size][kvd]
+    float *k, *v;               // pools [layer][page][page_size][kvd]; fp16 elements when f16
     const int32_t *page_table;  // [max_seqs][max_pages]
     int max_pages;
     int page_size;              // positions per page (power of two)
-    int64_t layer_stride;       // floats per layer in each pool
+    int64_t layer_stride;       // elements per layer in each pool
     int kvd;
+    int f16;                    // 1: the pools hold IEEE half (reduced-precision cache), 0: fp32
 };
 
 // QK-norm + RoPE on q (in place) and k, then append k, v to the cache

@@ -249,13 +249,17 @@ class Model:
 
 
 def Load(path: str, maxCtx: int = 0, engine: Optional[Engine] = None, max_seqs: int = 1,
-         device: int = 0) -> Model:
+         device: int = 0, kv_f16: bool = False) -> Model:
     """infer.Load (model.go:90-203) on a GGUF file path: parse, derive the
-    config, upload the blocks unchanged and build the device state."""
+    config, upload the blocks unchanged and build the device state.  kv_f16:
+    keep the KV cache in IEEE half (acm_engine_set_kv_f16; no reference
+    counterpart)."""
     own = engine is None
     e = engine or Engine(device)
     h = C.c_void_p()
+    _lib.lib().acm_engine_set_kv_f16(e.handle, 1 if kv_f16 else 0)
     rc = _lib.lib().acm_model_load_gguf(e.handle, path.encode(), maxCtx, max_seqs, C.byref(h))
+    _lib.lib().acm_engine_set_kv_f16(e.handle, 0)
     if rc:
         msg = _lib.lib().acm_engine_error(e.handle).decode()
         if own:

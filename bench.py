@@ -329,7 +329,7 @@ def run_serve(args, rank, world, local):
     path, _ = model_path(rank, world)
     torch.cuda.set_device(local)
     eng = acm.Engine(local)
-    m = acm.Load(path, SERVE_CTX, engine=eng, max_seqs=SERVE_BATCH + 1)
+    m = acm.Load(path, SERVE_CTX, engine=eng, max_seqs=SERVE_BATCH + 1, kv_f16=args.kv_f16)
     reqs = serve_requests()
     mine = [reqs[i] for i in partition(reqs, world)[rank]]
     batch = [(p, acm.Sampler(0.7, 40, 0.0, Seed=seed), SERVE_GEN) for p, seed in mine]
@@ -352,6 +352,7 @@ def run_serve(args, rank, world, local):
             "config": {"workload": f"{SERVE_N} requests, prompts U[300,1000] (seed 5), {SERVE_GEN} decode tokens, "
                                    f"top-k 40, T 0.7, seed 1000+i, <= {SERVE_BATCH} concurrent per GPU, "
                                    "longest-prompt-first partition over GPUs",
+                       "kv_cache": "f16" if args.kv_f16 else "f32",
                        "prefill_tokens": int(tot[0]), "decode_tokens": int(tot[1])},
             "data": "synthetic (random-init weights, seeded prompts)"}), flush=True)
     m.close()
@@ -528,6 +529,8 @@ def main():
                     help="run a short workload for the profiler instead of the benchmark")
     ap.add_argument("--tokens", type=int, default=8, help="decode tokens of --profile decode/trace")
     ap.add_argument("--type", choices=list(KB_TYPES), default="q4_k", help="weight type of --profile gemv")
+    ap.add_argument("--kv-f16", action="store_true",
+                    help="--workload serve with the reduced-precision (IEEE half) KV cache")
     ap.add_argument("--model", choices=list(MODELS), default="qwen3",
                     help="model shape of --profile prefill/decode/trace/load (qwen3: the benchmark's own)")
     ap.add_argument("--workload", choices=["single", "serve", "kernels"], default="single",

@@ -91,6 +91,17 @@ ACM_API int acm_open(int device, acm_engine **out);
 ACM_API int acm_close(acm_engine *e);
 ACM_API const char *acm_engine_error(acm_engine *e);
 
+/* No counterpart in the reference (its cache is fp32, model.go:353-360).
+ * Models created on this engine after the call keep their KV cache in IEEE
+ * half instead of fp32 (enable != 0): half the cache's HBM bytes and traffic,
+ * at the cost of rounding every cached key and value to 11 significant bits
+ * (the appended position is rounded before its own step uses it, so a
+ * position reads the same values in every step).  Logits then differ from
+ * the reference's fp32 path by more than rounding order; the measured
+ * deviation is stated with the tests that check it.  The persistent decode
+ * kernel (ACM_MEGA=1) is not used for such models.  Default: fp32. */
+ACM_API int acm_engine_set_kv_f16(acm_engine *e, int32_t enable);
+
 /* Create an empty model for `cfg`; replaces infer.Load's allocation part
  * (model.go:90-203).  max_seqs concurrent sequence slots, each up to
  * cfg->max_ctx positions. */
