@@ -13,6 +13,8 @@
 // (sum e*v, max, sum e) triples.
 #include <float.h>
 
+#include <algorithm>
+
 #include "attn_dev.cuh"
 #include "common.cuh"
 #include "kernels.h"
@@ -194,6 +196,266 @@ __global__ void __launch_bounds__(128) k_attn_decode(const RopeDesc r, const Att
                                                threadIdx.x, 1, j * hn, hn);
 }
 
+// ---------------------------------------------------------------------------
+// Batched decode attention (many tokens per launch, so that (token, kv head)
+// pairs alone fill the GPU): CTA (t, g, s) streams its range of token t's
+// context for the G query heads of kv head g in 32-position tiles,
+// double-buffered in shared memory in the cache's own format, with the
+// softmax maximum found as it goes (running maximum, sums and accumulators
+// rescaled by fastExp(m_old - m_new)) -- model.go:384-408.  The CTA whose
+// range holds the new position normalises and ropes the new key and appends
+// key and value to the cache before streaming.  With several splits, each
+// writes (sum e*v, max, sum e) and the last to arrive merges them.
+// ---------------------------------------------------------------------------
+constexpr int TT = 32;  // positions per tile
+
+__host__ __device__ constexpr int tiled_smem_floats(int HD, int G, int kt_bytes) {
+    // qs [G][HD+4] | K 2 x [TT][HD + 16/kt] | V 2 x [TT][HD] | sc [G][TT] | stat 3G+1 | gred [G][HD] | knew [HD] | flag
+    return (G * (HD + 4) + (2 * TT * (HD + 16 / kt_bytes) + 2 * TT * HD) * kt_bytes / 4 + G * TT + 4 * G +
+            (HD < 128 ? G * HD : 0) + HD + 4 + 3) & ~3;
+}
+
+__device__ __forceinline__ float kt_f(float v) { return v; }
+__device__ __forceinline__ float kt_f(__half v) { return __half2float(v); }
+
+template <int HD, typename KT>
+__global__ void __launch_bounds__(128) k_attn_decode_tiled(const RopeDesc r, const AttnDesc a, const KVDesc kv,
+                                                           int layer, TokMeta tm, int nsplit) {
+    extern __shared__ __align__(16) float sm[];
+    constexpr int PER = HD / 32, NR = (HD / 2 + 31) / 32, QS = HD + 4;
+    constexpr int EPR = 16 / (int)sizeof(KT);  // elements per 16-byte piece
+    constexpr int CPR = HD / EPR;              // pieces per row
+    constexpr int KSE = HD + EPR;              // K row stride (elements)
+    constexpr int GROUPS = 128 / HD, PS = dec_part_stride(HD);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int t = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
+    const int G = a.n_head / a.n_head_kv, nh = a.n_head, qd = nh * HD, kvd = a.n_head_kv * HD;
+    if (tid == 0) pdl_trigger();
+    pdl_wait();
+    const int seq = tm.seq[t], pos = tm.pos[t], L = pos + 1;
+    const int tiles_all = (L + TT - 1) / TT, tps = (tiles_all + nsplit - 1) / nsplit;
+    const int nsp = (tiles_all + tps - 1) / tps;  // splits this token uses
+    if (s >= nsp) return;
+    const int lo = s * tps * TT, hi = min(L, lo + tps * TT), ntile = (hi - lo + TT - 1) / TT;
+    float *qs = sm;
+    KT *kbuf = reinterpret_cast<KT *>(qs + G * QS);
+    KT *vbuf = kbuf + 2 * TT * KSE;
+    float *sc = reinterpret_cast<float *>(vbuf + 2 * TT * HD);
+    float *st_m = sc + G * TT, *st_l = st_m + G, *st_r = st_l + G;
+    float *gred = st_r + 2 * G;
+    float *knew = gred + (HD < 128 ? G * HD : 0);
+    int *flag = reinterpret_cast<int *>(knew + HD);
+    const int64_t lofs = (int64_t)layer * kv.layer_stride;
+    const int32_t *pt = kv.page_table + (int64_t)seq * kv.max_pages;
+    const KT *kpool = reinterpret_cast<const KT *>(kv.k), *vpool = reinterpret_cast<const KT *>(kv.v);
+    auto load_tile = [&](int ti, int buf) {  // a tile lies in one page (page size a multiple of TT)
+        const int p0 = lo + ti * TT, n = min(TT, hi - p0);
+        const int64_t base =
+            lofs + ((int64_t)pt[p0 / kv.page_size] * kv.page_size + (p0 % kv.page_size)) * kv.kvd + g * HD;
+        KT *kd = kbuf + buf * TT * KSE, *vd = vbuf + buf * TT * HD;
+        for (int i = tid; i < n * CPR; i += 128) {
+            const int p = i / CPR, c = i - p * CPR;
+            cp_async16(kd + p * KSE + c * EPR, kpool + base + (int64_t)p * kv.kvd + c * EPR);
+            cp_async16(vd + p * HD + c * EPR, vpool + base + (int64_t)p * kv.kvd + c * EPR);
+        }
+        cp_async_commit();
+    };
+    // ---- query heads, and the new key / value appended before streaming ----
+    const int half = r.rope_dim / 2;
+    const bool has_new = pos >= lo && pos < hi;
+    {
+        float nq[PER];
+        float2 cs[NR];
+#pragma unroll
+        for (int e = 0; e < PER; e++) nq[e] = r.q_nw ? r.q_nw[lane + 32 * e] : 0.f;
+#pragma unroll
+        for (int j = 0; j < NR; j++) {
+            const int i = lane + 32 * j;
+            cs[j] = i < half ? r.tab[(int64_t)pos * half + i] : make_float2(0.f, 0.f);
+        }
+        for (int h = warp; h < G; h += 4) {
+            float qv[PER];
+#pragma unroll
+            for (int e = 0; e < PER; e++) qv[e] = __ldcg(a.q + (int64_t)t * qd + (int64_t)(g * G + h) * HD + lane + 32 * e);
+            norm_rope_regs<HD, NR>(qs + h * QS, qv, r.q_nw != nullptr, nq, cs, half, r.interleaved, r.eps, lane);
+        }
+        if (has_new && warp == (G & 3)) {
+            float kx[PER], nk[PER], vx[PER];
+#pragma unroll
+            for (int e = 0; e < PER; e++) {
+                kx[e] = __ldcg(r.k + (int64_t)t * kvd + g * HD + lane + 32 * e);
+                vx[e] = __ldcg(r.v + (int64_t)t * kvd + g * HD + lane + 32 * e);
+                nk[e] = r.k_nw ? r.k_nw[lane + 32 * e] : 0.f;
+            }
+            norm_rope_regs<HD, NR>(knew, kx, r.k_nw != nullptr, nk, cs, half, r.interleaved, r.eps, lane);
+            const int64_t no = lofs + ((int64_t)pt[pos / kv.page_size] * kv.page_size + (pos % kv.page_size)) * kv.kvd +
+                               g * HD;
+#pragma unroll
+            for (int e = 0; e < PER; e++) {
+                kv_store(kv.k, no + lane + 32 * e, knew[lane + 32 * e], kv.f16);
+                kv_store(kv.v, no + lane + 32 * e, vx[e], kv.f16);
+            }
+            __threadfence();  // the row is read back through L2 by this CTA's tile copies
+        }
+        if (tid < G) {
+            st_m[tid] = -FLT_MAX;
+            st_l[tid] = 0.f;
+        }
+    }
+    __syncthreads();  // queries ready; the appended row visible to this CTA's copies
+    // ---- stream the tiles ----
+    const int d = tid % HD, gp = tid / HD;
+    float acc[8];
+#pragma unroll
+    for (int h = 0; h < 8; h++) acc[h] = 0.f;
+    load_tile(0, 0);
+    for (int ti = 0; ti < ntile; ti++) {
+        const int buf = ti & 1;
+        if (ti + 1 < ntile) {
+            load_tile(ti + 1, buf ^ 1);
+            cp_async_wait_group<1>();
+        } else {
+            cp_async_wait_group<0>();
+        }
+        __syncthreads();
+        const int n = min(TT, hi - (lo + ti * TT));
+        const KT *kt = kbuf + buf * TT * KSE, *vt = vbuf + buf * TT * HD;
+        // scores, one lane per (head, position); a head's 32 positions are one warp
+        for (int b0 = warp * 32; b0 < G * TT; b0 += 128) {
+            const int i = b0 + lane, h = i / TT, p = i - h * TT;
+            const bool in = i < G * TT, ok = in && p < n;
+            float sv = -FLT_MAX;
+            if (ok) {
+                const float *qh = qs + h * QS;
+                const KT *kp = kt + p * KSE;
+                float4 ac = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+                for (int d4 = 0; d4 < HD / 4; d4++) {
+                    const float4 x = *reinterpret_cast<const float4 *>(qh + 4 * d4);
+                    float y0, y1, y2, y3;
+                    if constexpr (sizeof(KT) == 4) {
+                        const float4 y = *reinterpret_cast<const float4 *>(kp + 4 * d4);
+                        y0 = y.x, y1 = y.y, y2 = y.z, y3 = y.w;
+                    } else {
+                        const uint2 hv = *reinterpret_cast<const uint2 *>(kp + 4 * d4);
+                        const float2 a0 = __half22float2(*reinterpret_cast<const __half2 *>(&hv.x));
+                        const float2 a1 = __half22float2(*reinterpret_cast<const __half2 *>(&hv.y));
+                        y0 = a0.x, y1 = a0.y, y2 = a1.x, y3 = a1.y;
+                    }
+                    ac.x = fmaf(x.x, y0, ac.x);
+                    ac.y = fmaf(x.y, y1, ac.y);
+                    ac.z = fmaf(x.z, y2, ac.z);
+                    ac.w = fmaf(x.w, y3, ac.w);
+                }
+                sv = __fmul_rn((ac.x + ac.y) + (ac.z + ac.w), a.scale);
+            }
+            if (in) {  // whole warps: every lane of a head's warp takes part
+                const float mold = st_m[h];
+                const float mnew = fmaxf(mold, warp_max(sv));
+                const float e = ok ? fast_exp(__fsub_rn(sv, mnew)) : 0.f;
+                const float sum = warp_sum(e);
+                sc[h * TT + p] = e;
+                if (p == 0) {
+                    const float rs = mold == -FLT_MAX ? 0.f : fast_exp(__fsub_rn(mold, mnew));
+                    st_r[h] = rs;
+                    st_m[h] = mnew;
+                    st_l[h] = fmaf(st_l[h], rs, sum);
+                }
+            }
+        }
+        __syncthreads();
+        // P.V with the running rescale
+#pragma unroll
+        for (int h = 0; h < 8; h++) {
+            if (h < G) {
+                const float *sh = sc + h * TT;
+                float a2 = acc[h] * st_r[h];
+#pragma unroll 4
+                for (int p = gp; p < n; p += GROUPS) a2 = fmaf(sh[p], kt_f(vt[p * HD + d]), a2);
+                acc[h] = a2;
+            }
+        }
+        __syncthreads();  // the tile's buffers are free for the load two tiles on
+    }
+    // ---- combine the position groups (HD < 128) ----
+    if (GROUPS > 1) {
+#pragma unroll
+        for (int h = 0; h < 8; h++)
+            if (h < G && gp > 0) gred[h * HD + d] = acc[h];
+        __syncthreads();
+        if (gp == 0) {
+#pragma unroll
+            for (int h = 0; h < 8; h++)
+                if (h < G) acc[h] += gred[h * HD + d];
+        }
+    }
+    if (nsp == 1) {
+        if (gp == 0) {
+#pragma unroll
+            for (int h = 0; h < 8; h++)
+                if (h < G) a.out[(int64_t)t * qd + (int64_t)(g * G + h) * HD + d] = acc[h] / st_l[h];
+        }
+        return;
+    }
+    if (gp == 0) {
+#pragma unroll
+        for (int h = 0; h < 8; h++) {
+            if (h < G) {
+                float *pp = a.part + (((int64_t)t * nh + g * G + h) * a.nsplit + s) * PS;
+                pp[d] = acc[h];
+                if (d == 0) {
+                    pp[HD] = st_m[h];
+                    pp[HD + 1] = st_l[h];
+                }
+            }
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        int *cnt = a.counter + (int64_t)t * nh + g * G;
+        const int old = atomicAdd(cnt, 1);
+        const int last = old == nsp - 1;
+        if (last) *cnt = 0;  // ready for the next step
+        *flag = last;
+    }
+    __syncthreads();
+    if (*flag) {  // the last split merges every split's rows (few: direct loads)
+        __threadfence();
+        for (int o = tid; o < G * HD; o += 128) {
+            const int h = o / HD, dd = o - h * HD;
+            const float *ph = a.part + ((int64_t)t * nh + g * G + h) * a.nsplit * PS;
+            float M = -FLT_MAX;
+            for (int c = 0; c < nsp; c++) M = fmaxf(M, __ldcg(ph + c * PS + HD));
+            float num = 0.f, den = 0.f;
+            for (int c = 0; c < nsp; c++) {
+                const float w = fast_exp(__fsub_rn(__ldcg(ph + c * PS + HD), M));
+                num = fmaf(w, __ldcg(ph + c * PS + dd), num);
+                den = fmaf(w, __ldcg(ph + c * PS + HD + 1), den);
+            }
+            a.out[(int64_t)t * qd + (int64_t)(g * G + h) * HD + dd] = num / den;
+        }
+    }
+}
+
+template <int HD, typename KT>
+static cudaError_t launch_tiled(const RopeDesc &r, const AttnDesc &a, const KVDesc &kv, int layer, TokMeta tm,
+                               int ntok, int nsplit, cudaStream_t st) {
+    const int G = a.n_head / a.n_head_kv;
+    const size_t smem = (size_t)tiled_smem_floats(HD, G, (int)sizeof(KT)) * sizeof(float);
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev & 63]) {
+        cudaError_t e = cudaFuncSetAttribute(k_attn_decode_tiled<HD, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             227 * 1024);
+        if (e != cudaSuccess) return e;
+        attr[dev & 63] = true;
+    }
+    return launch_pdl(k_attn_decode_tiled<HD, KT>, dim3(ntok, a.n_head_kv, nsplit), dim3(128), smem, st, r, a, kv,
+                      layer, tm, nsplit);
+}
+
 cudaError_t attention_decode_launch(const RopeDesc &r, const AttnDesc &a, const KVDesc &kv, int layer, TokMeta tm,
                                     int ntok, int max_pos, cudaStream_t st) {
     if (ntok <= 0) return cudaSuccess;
@@ -204,10 +466,23 @@ cudaError_t attention_decode_launch(const RopeDesc &r, const AttnDesc &a, const 
     if (kv.page_size % ATT_CHUNK) return cudaErrorInvalidValue;
     const int HD = a.head_dim;
     const size_t smem = (size_t)dec_item_floats(HD, ATT_CHUNK, G) * sizeof(float);
+    // Many (token, kv head) pairs: the streaming kernel, a few splits per pair.
+    const bool batched = (int64_t)ntok * a.n_head_kv * 4 >= (a.min_items > 1 ? a.min_items : 1);
+    if (batched && a.min_items > 0) {
+        const int target = 6 * a.min_items;  // ~3 resident CTAs per SM, two waves
+        int ns = (int)std::min<int64_t>(16, (target + (int64_t)ntok * a.n_head_kv - 1) / ((int64_t)ntok * a.n_head_kv));
+        ns = std::max(1, std::min(ns, a.nsplit));
+        cudaError_t e = kv.f16 ? (HD == 128 ? launch_tiled<128, __half>(r, a, kv, layer, tm, ntok, ns, st)
+                                            : launch_tiled<64, __half>(r, a, kv, layer, tm, ntok, ns, st))
+                               : (HD == 128 ? launch_tiled<128, float>(r, a, kv, layer, tm, ntok, ns, st)
+                                            : launch_tiled<64, float>(r, a, kv, layer, tm, ntok, ns, st));
+        if (e != cudaSuccess) return e;
+        return launched(1);
+    }
     // y: kv head x head subset (unused subsets exit).  Query heads are split
     // over items only while the launch has few (token, kv head) pairs: with
     // many tokens the extra CTAs would mostly exit at once.
-    const int nsub = (int64_t)ntok * a.n_head_kv * 4 >= (a.min_items > 1 ? a.min_items : 1) ? 1 : G;
+    const int nsub = batched ? 1 : G;
     dim3 grid(ntok, a.n_head_kv * nsub, nchunk);
     cudaError_t e = HD == 128 ? launch_pdl(k_attn_decode<128>, grid, dim3(128), smem, st, r, a, kv, layer, tm)
                               : launch_pdl(k_attn_decode<64>, grid, dim3(128), smem, st, r, a, kv, layer, tm);

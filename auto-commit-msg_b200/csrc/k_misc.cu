@@ -191,6 +191,92 @@ __device__ void bitonic_desc(uint64_t *s, int n) {
     }
 }
 
+// The TOPK_MAX largest keys of s[0..n) (0 = empty; n a power of two and a
+// multiple of 32), in descending order, into s[0..TOPK_MAX) (fewer non-empty
+// keys: the rest 0).  A radix select over the keys' high words (the logit's
+// order bits; 4 digits of 8 bits, most significant first) finds the high word
+// T of the TOPK_MAX-th largest key; the keys whose high word is >= T --
+// TOPK_MAX of them unless several logits equal that one -- are gathered into
+// `work` (n keys) and sorted, the full key (value, then lower index) deciding.
+// hist: 256 words; ctl: 4 ints.  Every thread of the block calls it.
+__device__ void block_top64(uint64_t *s, int n, uint64_t *work, uint32_t *hist, int *ctl) {
+    const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) ctl[0] = 0;
+    __syncthreads();
+    int local = 0;
+    for (int i = tid; i < n; i += nt) local += s[i] != 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
+    if (lane == 0 && local) atomicAdd(&ctl[0], local);
+    __syncthreads();
+    const int total = ctl[0];
+    uint32_t T = 0;
+    if (total > TOPK_MAX) {
+        uint32_t prefix = 0, pmask = 0;
+        int want = TOPK_MAX;  // rank sought among the keys that match the prefix
+        for (int dg = 3; dg >= 0; dg--) {
+            for (int i = tid; i < 256; i += nt) hist[i] = 0u;
+            __syncthreads();
+            for (int i = tid; i < n; i += nt) {  // n is a multiple of 32: whole warps iterate together
+                const uint64_t k = s[i];
+                const uint32_t h = (uint32_t)(k >> 32);
+                const uint32_t bin = (k && (h & pmask) == prefix) ? (h >> (8 * dg)) & 255u : 256u;
+                const unsigned same = __match_any_sync(0xffffffffu, bin);
+                if (bin < 256u && lane == __ffs(same) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(same));
+            }
+            __syncthreads();
+            if (warp == 0) {  // lane l: bins 255 - 8l down to 248 - 8l; ranks counted from the top
+                uint32_t c[8], tot = 0;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    c[j] = hist[255 - 8 * lane - j];
+                    tot += c[j];
+                }
+                uint32_t incl = tot;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += x;
+                }
+                const uint32_t excl = incl - tot, w = (uint32_t)want;
+                if (excl < w && w <= incl) {
+                    uint32_t acc = excl;
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        if (acc + c[j] >= w) {
+                            ctl[1] = 255 - 8 * lane - j;
+                            ctl[2] = (int)(w - acc);
+                            break;
+                        }
+                        acc += c[j];
+                    }
+                }
+            }
+            __syncthreads();
+            prefix |= (uint32_t)ctl[1] << (8 * dg);
+            pmask |= 0xFFu << (8 * dg);
+            want = ctl[2];
+            __syncthreads();
+        }
+        T = prefix;
+    }
+    if (tid == 0) ctl[3] = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += nt) {
+        const uint64_t k = s[i];
+        if (k && (uint32_t)(k >> 32) >= T) work[atomicAdd(&ctl[3], 1)] = k;
+    }
+    __syncthreads();
+    const int m = ctl[3];
+    int mp = TOPK_MAX;
+    while (mp < m) mp <<= 1;
+    for (int i = m + tid; i < mp; i += nt) work[i] = 0ull;
+    __syncthreads();
+    bitonic_desc(work, mp);
+    for (int i = tid; i < TOPK_MAX; i += nt) s[i] = work[i];
+    __syncthreads();
+}
+
 // Per chunk of SAMPLE_CHUNK logits: the top `kk` keys (kk = 1 or 64).
 __global__ void __launch_bounds__(256) k_topk_partial(const float *logits, const int32_t *rows, int64_t ld,
                                                       int vocab, int kk, uint64_t *cand, int nchunks) {
@@ -221,12 +307,15 @@ __global__ void __launch_bounds__(256) k_topk_partial(const float *logits, const
         }
         return;
     }
+    __shared__ uint64_t work[SAMPLE_CHUNK];
+    __shared__ uint32_t hist[256];
+    __shared__ int ctl[4];
     for (int i = threadIdx.x; i < SAMPLE_CHUNK; i += 256) {
         const int v = base + i;
         s[i] = v < vocab ? logit_key(lg[v], v) : 0ull;
     }
     __syncthreads();
-    bitonic_desc(s, SAMPLE_CHUNK);
+    block_top64(s, SAMPLE_CHUNK, work, hist, ctl);
     for (int i = threadIdx.x; i < TOPK_MAX; i += 256) out[i] = s[i];
 }
 
@@ -258,13 +347,17 @@ __global__ void __launch_bounds__(1024) k_sample_final(SampleDesc d, int kk) {
     extern __shared__ uint64_t s[];
     const int t = blockIdx.x;
     const int n = d.nchunks * kk;
-    int np = 1;
+    int np = 32;  // as the launch sized the shared memory
     while (np < n) np <<= 1;
     const uint64_t *cand = d.cand + (int64_t)t * d.nchunks * TOPK_MAX;
     for (int i = threadIdx.x; i < np; i += blockDim.x)
         s[i] = i < n ? cand[(i / kk) * TOPK_MAX + (i % kk)] : 0ull;
     __syncthreads();
-    if (kk > 1) bitonic_desc(s, np);
+    if (kk > 1) {
+        uint64_t *work = s + np;
+        uint32_t *hist = reinterpret_cast<uint32_t *>(work + np);
+        block_top64(s, np, work, hist, reinterpret_cast<int *>(hist + 256));
+    }
     if (threadIdx.x != 0) return;
     const double temp = d.temp ? d.temp[t] : 0.0;
     if (kk == 1 || temp <= 0.0) {
@@ -315,9 +408,10 @@ cudaError_t sample_launch(const SampleDesc &d, int ntok, bool all_greedy, cudaSt
     const int kk = all_greedy ? 1 : TOPK_MAX;
     dim3 g1(d.nchunks, ntok);
     launch_pdl(k_topk_partial, g1, dim3(256), 0, st, d.logits, d.rows, d.ld, d.vocab, kk, d.cand, d.nchunks);
-    int np = 1;
+    int np = 32;
     while (np < d.nchunks * kk) np <<= 1;
-    const size_t smem = (size_t)np * sizeof(uint64_t);
+    // keys, the top-64 gather buffer, histogram and control words
+    const size_t smem = kk > 1 ? 2 * (size_t)np * sizeof(uint64_t) + 256 * 4 + 16 : (size_t)np * sizeof(uint64_t);
     static bool attr[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);

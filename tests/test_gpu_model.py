@@ -177,6 +177,40 @@ def test_batched_decode_matches_single(acm, eng, oracle, synth, tiny_models):
     m.close()
 
 
+@pytest.mark.parametrize("name,nseq,kv_f16", [("qwen3", 24, False), ("qwen2", 40, False), ("llama_q5", 24, False),
+                                              ("qwen3", 24, True)])
+def test_batched_decode_streaming_attention(acm, eng, oracle, synth, tiny_models, name, nseq, kv_f16):
+    """Enough (token, kv head) pairs in one decode step that attention takes
+    the streaming kernel (32-position tiles, running softmax, a few splits per
+    pair): every slot's logits against its own oracle run, over contexts of
+    1 to 7 tiles (GQA groups of 2 and 4, head dims 128 and 64; fp32 and half
+    caches -- the half cache against the fp32 oracle within its stated
+    deviation)."""
+    tol = 1e-3 if kv_f16 else 1e-4
+    path = tiny_models[name]
+    m = acm.Load(path, 0, engine=eng, max_seqs=nseq, kv_f16=kv_f16)
+    seqs = [m.seq] + [m.open_seq() for _ in range(nseq - 1)]
+    rng = np.random.default_rng(nseq)
+    lens = [int(n) for n in rng.integers(1, 220, nseq)]
+    oracles = [oracle.Model(path, 0) for _ in seqs]
+    toks = []
+    for s, n, o in zip(seqs, lens, oracles):
+        p = synth.prompt_ids(n, m.Cfg.vocab, 900 + n)
+        lg, lo = m.Forward(p, seq=s), o.forward(p)
+        toks.append(int(np.argmax(lo)))
+    samplers = [acm.Sampler(0.0)] * nseq
+    for step in range(4):
+        out, lgs = m.decode_step(seqs, toks, samplers, [step + 1] * nseq, want_logits=True)
+        nxt = []
+        for i, o in enumerate(oracles):
+            lo = o.forward([toks[i]])
+            assert rel_l2(lgs[i], lo) < tol, (i, lens[i], step)
+            nxt.append(int(np.argmax(lo)))  # teacher forcing
+        toks = nxt
+    assert [m.Pos(s) for s in seqs] == [n + 4 for n in lens]
+    m.close()
+
+
 def test_add_tensor_boundary(acm, eng, oracle, synth, tiny_models):
     """The low-level boundary a cgo shim uses: create + add_tensor per GGUF
     tensor (bytes unchanged) + finalize gives the same logits as Load."""

@@ -30,11 +30,11 @@ def eng(acm):
     e.close()
 
 
-@pytest.mark.parametrize("max_batch", [4, 12])
+@pytest.mark.parametrize("max_batch", [4, 12, 24])
 def test_serve_greedy_matches_oracle(acm, eng, oracle, synth, tiny_models, max_batch):
     path = tiny_models["qwen3"]
     m = acm.Load(path, 0, engine=eng, max_seqs=max_batch + 1)
-    reqs = _requests(synth, m.Cfg.vocab, lambda i: acm.Sampler(0.0), n=14, seed=max_batch)
+    reqs = _requests(synth, m.Cfg.vocab, lambda i: acm.Sampler(0.0), n=max(14, max_batch + 6), seed=max_batch)
     res = m.Serve(reqs, max_batch=max_batch, stop_on_eos=False)
     assert m.Stats.PrefillToks == sum(len(p) for p, _, _ in reqs)
     assert m.Stats.DecodeToks == sum(t for _, _, t in reqs)
