@@ -474,6 +474,18 @@ def run_profile(args):
         return
     path, prompt = model_path(0, 1, args.model)
     eng = acm.Engine(0)
+    if args.profile == "serve":
+        # the first 64 requests of the many-request workload, `--tokens` decode
+        # tokens each: one prefill per request, then 64-token decode steps
+        m = acm.Load(path, SERVE_CTX, engine=eng, max_seqs=SERVE_BATCH + 1, kv_f16=args.kv_f16)
+        reqs = [(p, acm.Sampler(0.7, 40, 0.0, Seed=seed), args.tokens) for p, seed in serve_requests()[:SERVE_BATCH]]
+        m.Serve(reqs, max_batch=SERVE_BATCH, stop_on_eos=False)
+        st = m.Stats
+        print(f"serve {len(reqs)} requests: decode {st.DecodeToks / st.Decode:.1f} tok/s, "
+              f"prefill {st.PrefillToks / st.Prefill:.1f} tok/s", flush=True)
+        m.close()
+        eng.close()
+        return
     if args.profile == "load":
         for i in range(3):  # GGUF parse + upload of every tensor + finalize, wall clock
             t0 = time.perf_counter()
@@ -525,12 +537,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--profile", choices=["prefill", "decode", "trace", "load", "gemv"],
+    ap.add_argument("--profile", choices=["prefill", "decode", "trace", "load", "gemv", "serve"],
                     help="run a short workload for the profiler instead of the benchmark")
     ap.add_argument("--tokens", type=int, default=8, help="decode tokens of --profile decode/trace")
     ap.add_argument("--type", choices=list(KB_TYPES), default="q4_k", help="weight type of --profile gemv")
     ap.add_argument("--kv-f16", action="store_true",
-                    help="--workload serve with the reduced-precision (IEEE half) KV cache")
+                    help="--workload serve / --profile serve with the reduced-precision (IEEE half) KV cache")
     ap.add_argument("--model", choices=list(MODELS), default="qwen3",
                     help="model shape of --profile prefill/decode/trace/load (qwen3: the benchmark's own)")
     ap.add_argument("--workload", choices=["single", "serve", "kernels"], default="single",
