@@ -18,6 +18,11 @@ template <> struct SpanBytes<T_Q6_K> { static constexpr int v = 210; };
 template <> struct SpanBytes<T_Q8_0> { static constexpr int v = 272; };
 template <> struct SpanBytes<T_F16> { static constexpr int v = 512; };
 
+// Byte b of v in the low mantissa bits of 2^23: the float 2^23 + byte.
+__device__ __forceinline__ float byte_m23(uint32_t v, int b) {
+    return __int_as_float(__byte_perm(v, 0x4B000000u, 0x7540u | (uint32_t)b));
+}
+
 template <int T>
 __host__ __device__ constexpr bool sb_supported() {
     return T == T_Q4_K || T == T_Q5_K || T == T_Q6_K || T == T_Q8_0 || T == T_F16;
@@ -42,9 +47,12 @@ __device__ __forceinline__ void sb_dot(const uint8_t *blk, const float *x256, in
             const uint8_t *qs = blk + (T == T_Q4_K ? 16 : 48) + 32 * g;
             const uint4 qa = *reinterpret_cast<const uint4 *>(qs), qb = *reinterpret_cast<const uint4 *>(qs + 16);
             const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-            float slo[MT], shi[MT];
+            // packed two-lane fp32 (sm_100 FADD2 / FFMA2): element pairs share one
+            // instruction; each accumulator pair holds the even / odd elements
+            float2 slo2[MT], shi2[MT];
 #pragma unroll
-            for (int m = 0; m < MT; m++) slo[m] = shi[m] = 0.f;
+            for (int m = 0; m < MT; m++) slo2[m] = shi2[m] = make_float2(0.f, 0.f);
+            const float2 nmag = make_float2(-MAGIC, -MAGIC);
 #pragma unroll
             for (int w = 0; w < 8; w++) {
                 uint32_t lo, hi;
@@ -56,26 +64,27 @@ __device__ __forceinline__ void sb_dot(const uint8_t *blk, const float *x256, in
                     lo = (qw[w] & 0x0F0F0F0Fu) | (((hw[w] >> (2 * g)) & 0x01010101u) << 4);
                     hi = ((qw[w] >> 4) & 0x0F0F0F0Fu) | (((hw[w] >> (2 * g + 1)) & 0x01010101u) << 4);
                 }
-                float fl[4], fh[4];
-#pragma unroll
-                for (int b = 0; b < 4; b++) {
-                    fl[b] = byte_f(lo, b, MAGIC);
-                    fh[b] = byte_f(hi, b, MAGIC);
-                }
+                // bytes into the low mantissa of 2^23, then minus 2^23: the exact integers
+                const float2 fl01 = __fadd2_rn(make_float2(byte_m23(lo, 0), byte_m23(lo, 1)), nmag);
+                const float2 fl23 = __fadd2_rn(make_float2(byte_m23(lo, 2), byte_m23(lo, 3)), nmag);
+                const float2 fh01 = __fadd2_rn(make_float2(byte_m23(hi, 0), byte_m23(hi, 1)), nmag);
+                const float2 fh23 = __fadd2_rn(make_float2(byte_m23(hi, 2), byte_m23(hi, 3)), nmag);
 #pragma unroll
                 for (int m = 0; m < MT; m++)
                     if (m < m_used) {
                         const float4 xl = *reinterpret_cast<const float4 *>(x256 + m * xstr + 64 * g + 4 * w);
                         const float4 xh = *reinterpret_cast<const float4 *>(x256 + m * xstr + 64 * g + 32 + 4 * w);
-                        slo[m] = fmaf(fl[0], xl.x, slo[m]);
-                        slo[m] = fmaf(fl[1], xl.y, slo[m]);
-                        slo[m] = fmaf(fl[2], xl.z, slo[m]);
-                        slo[m] = fmaf(fl[3], xl.w, slo[m]);
-                        shi[m] = fmaf(fh[0], xh.x, shi[m]);
-                        shi[m] = fmaf(fh[1], xh.y, shi[m]);
-                        shi[m] = fmaf(fh[2], xh.z, shi[m]);
-                        shi[m] = fmaf(fh[3], xh.w, shi[m]);
+                        slo2[m] = __ffma2_rn(fl01, make_float2(xl.x, xl.y), slo2[m]);
+                        slo2[m] = __ffma2_rn(fl23, make_float2(xl.z, xl.w), slo2[m]);
+                        shi2[m] = __ffma2_rn(fh01, make_float2(xh.x, xh.y), shi2[m]);
+                        shi2[m] = __ffma2_rn(fh23, make_float2(xh.z, xh.w), shi2[m]);
                     }
+            }
+            float slo[MT], shi[MT];
+#pragma unroll
+            for (int m = 0; m < MT; m++) {
+                slo[m] = slo2[m].x + slo2[m].y;
+                shi[m] = shi2[m].x + shi2[m].y;
             }
             const float d1 = d * sc0, m1 = dmin * mn0, m2 = dmin * mn1;
             const float d2 = (T == T_Q4_K) ? d * sc1 * 0.0625f : d * sc1;
