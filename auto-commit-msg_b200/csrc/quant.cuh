@@ -58,6 +58,10 @@ __device__ __forceinline__ float byte_f(uint32_t v, int b, float off_plus_magic)
     return __int_as_float(__byte_perm(v, 0x4B000000u, 0x7540u | (uint32_t)b)) - off_plus_magic;
 }
 constexpr float MAGIC = 8388608.0f;  // 2^23
+// Byte b of v in the low mantissa bits of 2^23: the float 2^23 + byte.
+__device__ __forceinline__ float byte_m23(uint32_t v, int b) {
+    return __int_as_float(__byte_perm(v, 0x4B000000u, 0x7540u | (uint32_t)b));
+}
 
 // scaleMinK4, tensor.go:123-130, for a runtime index j and the 12 scale
 // bytes held in three words.
@@ -270,9 +274,12 @@ __device__ __forceinline__ void unit_dot(const uint8_t *row, int u, int K, const
             qhv = *reinterpret_cast<const uint4 *>(blk + 16 + 16 * half);
         }
         const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
-        float slo[MT], shi[MT];
+        // packed two-lane fp32 (sm_100 FADD2 / FFMA2): half the instructions and
+        // half the length of each accumulation chain (even / odd elements)
+        float2 slo2[MT], shi2[MT];
 #pragma unroll
-        for (int m = 0; m < MT; m++) slo[m] = shi[m] = 0.f;
+        for (int m = 0; m < MT; m++) slo2[m] = shi2[m] = make_float2(0.f, 0.f);
+        const float2 nmag = make_float2(-MAGIC, -MAGIC);
 #pragma unroll
         for (int w = 0; w < 4; w++) {
             uint32_t lo, hi;
@@ -284,26 +291,26 @@ __device__ __forceinline__ void unit_dot(const uint8_t *row, int u, int K, const
                 lo = (qw[w] & 0x0F0F0F0Fu) | (((qhw[w] >> (2 * g)) & 0x01010101u) << 4);
                 hi = ((qw[w] >> 4) & 0x0F0F0F0Fu) | (((qhw[w] >> (2 * g + 1)) & 0x01010101u) << 4);
             }
-            float fl[4], fh[4];
-#pragma unroll
-            for (int b = 0; b < 4; b++) {
-                fl[b] = byte_f(lo, b, MAGIC);
-                fh[b] = byte_f(hi, b, MAGIC);
-            }
+            const float2 fl01 = __fadd2_rn(make_float2(byte_m23(lo, 0), byte_m23(lo, 1)), nmag);
+            const float2 fl23 = __fadd2_rn(make_float2(byte_m23(lo, 2), byte_m23(lo, 3)), nmag);
+            const float2 fh01 = __fadd2_rn(make_float2(byte_m23(hi, 0), byte_m23(hi, 1)), nmag);
+            const float2 fh23 = __fadd2_rn(make_float2(byte_m23(hi, 2), byte_m23(hi, 3)), nmag);
 #pragma unroll
             for (int m = 0; m < MT; m++) {
                 if (m < m_used) {
                     float4 xl = xv.chunk(m, w), xh = xv.chunk(m, 4 + w);
-                    slo[m] = fmaf(fl[0], xl.x, slo[m]);
-                    slo[m] = fmaf(fl[1], xl.y, slo[m]);
-                    slo[m] = fmaf(fl[2], xl.z, slo[m]);
-                    slo[m] = fmaf(fl[3], xl.w, slo[m]);
-                    shi[m] = fmaf(fh[0], xh.x, shi[m]);
-                    shi[m] = fmaf(fh[1], xh.y, shi[m]);
-                    shi[m] = fmaf(fh[2], xh.z, shi[m]);
-                    shi[m] = fmaf(fh[3], xh.w, shi[m]);
+                    slo2[m] = __ffma2_rn(fl01, make_float2(xl.x, xl.y), slo2[m]);
+                    slo2[m] = __ffma2_rn(fl23, make_float2(xl.z, xl.w), slo2[m]);
+                    shi2[m] = __ffma2_rn(fh01, make_float2(xh.x, xh.y), shi2[m]);
+                    shi2[m] = __ffma2_rn(fh23, make_float2(xh.z, xh.w), shi2[m]);
                 }
             }
+        }
+        float slo[MT], shi[MT];
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            slo[m] = slo2[m].x + slo2[m].y;
+            shi[m] = shi2[m].x + shi2[m].y;
         }
         const float d1 = d * sc0, m1 = dmin * mn0, m2 = dmin * mn1;
         const float d2 = (T == T_Q4_K) ? d * sc1 * 0.0625f : d * sc1;

@@ -18,11 +18,6 @@ template <> struct SpanBytes<T_Q6_K> { static constexpr int v = 210; };
 template <> struct SpanBytes<T_Q8_0> { static constexpr int v = 272; };
 template <> struct SpanBytes<T_F16> { static constexpr int v = 512; };
 
-// Byte b of v in the low mantissa bits of 2^23: the float 2^23 + byte.
-__device__ __forceinline__ float byte_m23(uint32_t v, int b) {
-    return __int_as_float(__byte_perm(v, 0x4B000000u, 0x7540u | (uint32_t)b));
-}
-
 template <int T>
 __host__ __device__ constexpr bool sb_supported() {
     return T == T_Q4_K || T == T_Q5_K || T == T_Q6_K || T == T_Q8_0 || T == T_F16;
