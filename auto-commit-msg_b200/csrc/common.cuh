@@ -39,14 +39,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait: gives up after ~2^22 polls (seconds), records the timeout
-// and returns false so the caller can unwind instead of hanging the GPU.
+// Bounded wait: gives up after `limit` polls, records the timeout and returns
+// false so the caller can unwind instead of hanging the GPU.  mbar_wait uses
+// the limit in g_wait_limit (default WAIT_LIMIT, ~2^22 polls: seconds; the
+// host may lower it, see set_wait_limit).
 constexpr uint32_t WAIT_LIMIT = 1u << 22;
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-    for (uint32_t it = 0; it < WAIT_LIMIT; ++it)
+extern __device__ uint32_t g_wait_limit;
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t *bar, uint32_t parity, uint32_t limit) {
+    for (uint32_t it = 0; it < limit; ++it)
         if (mbar_try_wait(bar, parity)) return true;
     atomicExch(&g_dev_error, DEV_ERR_TIMEOUT);
     return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    return mbar_wait_limit(bar, parity, *(volatile uint32_t *)&g_wait_limit);
+}
+
+// Order this thread's earlier generic-proxy accesses of shared memory before
+// its later async-proxy (bulk copy) writes into the same bytes.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // 1-D bulk copy global -> shared, completion counted on an mbarrier.

@@ -173,6 +173,8 @@ struct acm_model {
     DecPhase *d_dtable = nullptr;
     unsigned *d_bar = nullptr;
     unsigned long long *d_trace = nullptr;  // phase timestamps of the persistent kernel (tracing on)
+    unsigned long long *d_gtrace = nullptr; // per-CTA timelines of batch-1 GEMV launches (tracing on)
+    int gtrace_slots = 0, gtrace_on = 0;
     bool trace = false;
     int nchunks = 0;
     Pinned<int32_t> h_tok, h_seq, h_pos, h_out, h_topk, h_hist;
@@ -1196,6 +1198,7 @@ ACM_API int acm_model_finalize(acm_model *m) {
 }
 
 ACM_API int acm_model_destroy(acm_model *m) {
+    if (m && m->gtrace_on) gemv1_trace(nullptr, 0);
     if (!m) return ACM_ERR_INVALID;
     cudaSetDevice(m->e->device);
     cudaStreamSynchronize(m->e->stream);
@@ -1709,6 +1712,32 @@ ACM_API int acm_model_trace_read(acm_model *m, uint64_t *out, int64_t cap, int32
     CK_M(cudaMemcpy(out, m->d_trace, sizeof(uint64_t) * n, cudaMemcpyDeviceToHost));
     if (nblocks) *nblocks = m->dplan.grid;
     if (nphases) *nphases = m->dplan.nph;
+    return ACM_OK;
+}
+
+ACM_API int acm_model_trace_gemv(acm_model *m, int32_t slots) {
+    if (!m || !m->finalized || slots < 0) return set_err(m, ACM_ERR_INVALID, "bad arguments");
+    cudaSetDevice(m->e->device);
+    if (slots > m->gtrace_slots) {
+        CK_M(dalloc(m, &m->d_gtrace, (size_t)slots * 160 * 8));
+        m->gtrace_slots = slots;
+    }
+    if (slots) CK_M(cudaMemset(m->d_gtrace, 0, sizeof(unsigned long long) * (size_t)slots * 160 * 8));
+    m->gtrace_on = slots;
+    // captured graphs bake each launch's slot in: rebuild them
+    for (auto &g : m->graphs) cudaGraphExecDestroy(g.second.exec);
+    m->graphs.clear();
+    gemv1_trace(slots ? m->d_gtrace : nullptr, slots);
+    return ACM_OK;
+}
+
+ACM_API int acm_model_trace_gemv_read(acm_model *m, uint64_t *out, int64_t cap, int32_t *used) {
+    if (!m || !m->gtrace_on || !out) return set_err(m, ACM_ERR_INVALID, "GEMV tracing not enabled");
+    cudaSetDevice(m->e->device);
+    const int n = std::min(gemv1_trace_used(), m->gtrace_on);
+    if (cap < (int64_t)n * 160 * 8) return set_err(m, ACM_ERR_INVALID, "trace buffer too small");
+    CK_M(cudaMemcpy(out, m->d_gtrace, sizeof(uint64_t) * (size_t)n * 160 * 8, cudaMemcpyDeviceToHost));
+    if (used) *used = n;
     return ACM_OK;
 }
 

@@ -310,6 +310,19 @@ constexpr int DEC_CHUNK = 16;  // attention chunk of the persistent kernel (posi
 
 // Device error flag (timeouts in bounded waits).
 int read_and_clear_dev_error();
+// Polls a bounded mbarrier wait makes before it records a timeout (the
+// device default is WAIT_LIMIT of common.cuh); applies to the current device.
+cudaError_t set_wait_limit(uint32_t polls);
+constexpr uint32_t WAIT_LIMIT_DEFAULT = 1u << 22;
+
+// Batch-1 decode GEMV (k_gemv1.cu): activations in registers, lean CTAs.
+bool gemv1_supported(int type, int64_t k);
+cudaError_t gemv1_launch(const GemvSegDesc *segs, int nseg, const float *x, int64_t k, const float *norm_w,
+                         float eps, int num_sms, cudaStream_t st);
+// Per-CTA timelines of batch-1 GEMV launches (profiling): launches planned
+// while buf is set take consecutive slots of 160 CTAs x 8 stamps; null: off.
+void gemv1_trace(unsigned long long *buf, int slots);
+int gemv1_trace_used();
 
 // Count of kernels this library has launched (graph replays add the kernels
 // the graph holds); every launcher returns through launched().

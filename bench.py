@@ -152,9 +152,25 @@ class Clocks:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def cpu_baseline(path, prompt, nthreads=0, decode_tokens=8):
+def cpu_model():
+    """Host CPU model name and core count (recorded beside every CPU figure)."""
+    name = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    name = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return name, os.cpu_count()
+
+
+def cpu_baseline(path, prompt, nthreads=0, decode_tokens=GEN_TOKENS):
     """The oracle (a C restatement of the reference's AVX2 CPU path) on the
-    host cores: prefill of the 389-token prompt + `decode_tokens` greedy steps."""
+    host cores: one Generate of the workload (prefill of the 389-token prompt
+    + `decode_tokens` greedy steps).  Also returns its ids, the parity check
+    of the device's output."""
     import oracle as O
     O.set_threads(nthreads)
     m = O.Model(path, CTX)
@@ -162,7 +178,12 @@ def cpu_baseline(path, prompt, nthreads=0, decode_tokens=8):
     st = r["stats"]
     m.close()
     return {"decode_tok_s": st["decode_toks"] / st["decode_s"], "prefill_tok_s": st["prefill_toks"] / st["prefill_s"],
-            "cores": O.threads(), "seconds": st["decode_s"] + st["prefill_s"]}
+            "cores": O.threads(), "seconds": st["decode_s"] + st["prefill_s"], "ids": [int(i) for i in r["ids"]]}
+
+
+# The reference arm times a bounded number of full Generates (each ~6 s of
+# CPU work on 16 cores): the whole --steps/--warmup run stays within a minute.
+REF_STEPS, REF_WARMUP = 4, 1
 
 
 def run_reference(args, rank, world):
@@ -172,24 +193,28 @@ def run_reference(args, rank, world):
     import oracle as O
     O.set_threads(0)
     m = O.Model(path, CTX)
+    steps, warmup = min(args.steps, REF_STEPS), min(args.warmup, REF_WARMUP)
     dec_tok, dec_s, pre_tok, pre_s = 0, 0.0, 0, 0.0
-    for i in range(args.warmup + args.steps):
+    for i in range(warmup + steps):
         m.reset()
-        r = m.generate(prompt, max_tok=8, stop_on_eos=False)
-        if i >= args.warmup:
+        r = m.generate(prompt, max_tok=GEN_TOKENS, stop_on_eos=False)
+        if i >= warmup:
             dec_tok += r["stats"]["decode_toks"]
             dec_s += r["stats"]["decode_s"]
             pre_tok += r["stats"]["prefill_toks"]
             pre_s += r["stats"]["prefill_s"]
     v = dec_tok / dec_s
-    sample = f"per step: prefill {PROMPT_LEN} tokens + 8 greedy decode tokens (of the 64-token workload)"
+    cpu, ncpu = cpu_model()
+    sample = (f"{steps} timed Generates after {warmup} warm-up (of --steps {args.steps} / --warmup {args.warmup}), "
+              f"each the full workload: prefill {PROMPT_LEN} tokens + {GEN_TOKENS} greedy decode tokens")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "tok/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * (dec_s + pre_s) / args.steps, 3),
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * (dec_s + pre_s) / steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "prefill_tok_s": round(pre_tok / pre_s, 3),
         "config": {"workload": WORKLOAD, "impl": "CPU restatement of the reference's AVX2 path (oracle/)"},
-        "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": O.threads(), "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": O.threads(), "kind": "port",
+                         "cpu": cpu, "nproc": ncpu, "sample": sample},
         "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -271,16 +296,23 @@ def run_ours(args, rank, world, local):
         "roofline": {"bound": "hbm", "kernel": "k_gemv (all GEMV launches of one decode token)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "bytes_per_pass": int(nbytes), "launches_per_pass": nl, "traffic": traffic},
+                     "bytes_per_pass": int(nbytes), "launches_per_pass": nl, "traffic": traffic,
+                     "traffic_source": "profiles/traffic.json (DRAM bytes of the same pass, one ncu capture)"},
         "prefill_roofline": prefill_roof,
         "gpu_launches": tot_launches,
         "clocks": ck,
     }
     if world == 1 and rank == 0 and not args.no_cpu:
         cb = cpu_baseline(path, prompt)
+        cpu, ncpu = cpu_model()
         line["cpu_baseline"] = {"value": round(cb["decode_tok_s"], 3), "unit": "tok/s", "cores": cb["cores"],
-                                "kind": "port", "prefill_tok_s": round(cb["prefill_tok_s"], 2),
-                                "sample": f"prefill {PROMPT_LEN} tokens + 8 greedy decode tokens, oracle/ on all host threads"}
+                                "kind": "port", "prefill_tok_s": round(cb["prefill_tok_s"], 2), "cpu": cpu,
+                                "nproc": ncpu,
+                                "sample": f"one Generate: prefill {PROMPT_LEN} tokens + {GEN_TOKENS} greedy decode "
+                                          "tokens, oracle/ on all host threads"}
+        # parity of what was timed: the first timed Generate's ids against the oracle's
+        line["parity"] = {"ids_equal": first == cb["ids"], "steps": GEN_TOKENS,
+                          "first_diff": next((i for i, (a, b) in enumerate(zip(first, cb["ids"])) if a != b), None)}
     if rank == 0:
         print(json.dumps(line), flush=True)
     m.close()
@@ -497,6 +529,39 @@ def run_profile(args):
         eng.close()
         return
     m = acm.Load(path, CTX, engine=eng)
+    if args.profile == "gtrace":
+        # per-CTA timelines of the batch-1 GEMV launches of the last decode token
+        slots = 400
+        if lib.acm_model_trace_gemv(m.handle, slots):
+            raise RuntimeError(lib.acm_last_error(m.handle).decode())
+        m.Generate(prompt, acm.Sampler(0.0), args.tokens, stop_on_eos=False)
+        print(f"decode {args.tokens} tokens: {args.tokens / m.Stats.Decode:.1f} tok/s", flush=True)
+        buf = (C.c_uint64 * (slots * 160 * 8))()
+        used = C.c_int32()
+        if lib.acm_model_trace_gemv_read(m.handle, buf, slots * 160 * 8, C.byref(used)):
+            raise RuntimeError(lib.acm_last_error(m.handle).decode())
+        t = np.frombuffer(buf, dtype=np.uint64)[: used.value * 160 * 8].reshape(used.value, 160, 8).astype(np.int64)
+        per_tok = 4 * m.Cfg.n_layers + 1
+        t = t[used.value - per_tok: used.value]
+        valid = t[:, :, 0] > 0
+        base = t[:, :, 0][valid].min()
+        names = ["qkv", "o", "gateup", "down"] * m.Cfg.n_layers + ["lm_head"]
+        prev_end = None
+        for i in range(per_tok):
+            v = valid[i]
+            r = t[i][v]
+            st = lambda c: (r[:, c] - base) / 1e3
+            sm = np.bincount(r[:, 6].astype(np.int64), minlength=148)
+            end = st(5).max()
+            print(f"{i:3d} {names[i]:8s} ctas {v.sum():3d} sms {np.count_nonzero(sm):3d} max/sm {sm.max()}  "
+                  f"entry {st(0).min():8.2f}..{st(0).max():8.2f}  wait_over {st(2).min():8.2f}..{st(2).max():8.2f}  "
+                  f"x {st(3).max():8.2f}  w {st(4).min():8.2f}..{st(4).max():8.2f}  done {st(5).min():8.2f}..{end:8.2f}"
+                  + (f"  gap {st(2).min() - prev_end:6.2f}" if prev_end is not None else ""))
+            prev_end = end
+        lib.acm_model_trace_gemv(m.handle, 0)
+        m.close()
+        eng.close()
+        return
     if args.profile == "prefill":
         for i in range(3):
             m.Forward(prompt)
@@ -537,7 +602,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--profile", choices=["prefill", "decode", "trace", "load", "gemv", "serve"],
+    ap.add_argument("--profile", choices=["prefill", "decode", "trace", "gtrace", "load", "gemv", "serve"],
                     help="run a short workload for the profiler instead of the benchmark")
     ap.add_argument("--tokens", type=int, default=8, help="decode tokens of --profile decode/trace")
     ap.add_argument("--type", choices=list(KB_TYPES), default="q4_k", help="weight type of --profile gemv")

@@ -262,6 +262,15 @@ ACM_API uint64_t acm_kernel_launches(void);
  * acm_model_trace_read copies the last step's [nblocks][nphases][2] values. */
 ACM_API int acm_model_trace(acm_model *m, int32_t enable);
 ACM_API int acm_model_trace_read(acm_model *m, uint64_t *out, int64_t cap, int32_t *nblocks, int32_t *nphases);
+/* Tracing of the batch-1 decode GEMV launches, no reference counterpart:
+ * with slots > 0, decode graphs are rebuilt so that each batch-1 GEMV launch
+ * of a step takes one slot (in launch order) of 160 CTAs x 8 values: the
+ * %globaltimer ns at CTA entry, weights copy issued, dependency wait over,
+ * activations staged, first weights landed, rows done, then the SM id;
+ * slots = 0 turns it off.  acm_model_trace_gemv_read copies the slots the
+ * last capture used ([used][160][8]). */
+ACM_API int acm_model_trace_gemv(acm_model *m, int32_t slots);
+ACM_API int acm_model_trace_gemv_read(acm_model *m, uint64_t *out, int64_t cap, int32_t *used);
 
 /* Measurement helper, no reference counterpart: the tensor-core GEMM
  * launches of one ntok-token prefill (q/k/v, o, gate/up, down of every layer:
