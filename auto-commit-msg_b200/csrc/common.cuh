@@ -44,15 +44,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // the limit in g_wait_limit (default WAIT_LIMIT, ~2^22 polls: seconds; the
 // host may lower it, see set_wait_limit).
 constexpr uint32_t WAIT_LIMIT = 1u << 22;
-extern __device__ uint32_t g_wait_limit;
+extern __constant__ uint32_t g_wait_limit;
 __device__ __forceinline__ bool mbar_wait_limit(uint64_t *bar, uint32_t parity, uint32_t limit) {
     for (uint32_t it = 0; it < limit; ++it)
         if (mbar_try_wait(bar, parity)) return true;
     atomicExch(&g_dev_error, DEV_ERR_TIMEOUT);
     return false;
 }
+// The limit is read (constant cache) only when the phase has not completed
+// at the first test; a zero limit makes every wait give up at once.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-    return mbar_wait_limit(bar, parity, *(volatile uint32_t *)&g_wait_limit);
+    const uint32_t limit = g_wait_limit;
+    if (limit && mbar_try_wait(bar, parity)) return true;
+    return mbar_wait_limit(bar, parity, limit);
 }
 
 // Order this thread's earlier generic-proxy accesses of shared memory before

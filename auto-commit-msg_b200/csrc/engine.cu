@@ -672,6 +672,7 @@ int mega_step(acm_model *m, bool greedy) {
     A.area_off = m->dplan.area_off;
     A.meta_off = m->dplan.meta_off;
     A.attn_group_floats = m->dplan.attn_group_floats;
+    A.part_rows = m->dplan.part_rows;
     A.r = RopeDesc{m->q, m->k, m->v, nullptr, nullptr, m->rope_tab, c.n_head, c.n_head_kv, hd, c.rope_dim,
                    c.rope_interleaved, c.rms_eps};
     A.a = AttnDesc{m->q, m->att, c.n_head, c.n_head_kv, hd, 1.0f / (float)sqrt((double)hd), m->part,
@@ -1692,8 +1693,8 @@ ACM_API int acm_model_trace(acm_model *m, int32_t enable) {
     cudaSetDevice(m->e->device);
     if (enable && !mega_ready(m)) return set_err(m, ACM_ERR_INVALID, "persistent decode kernel not available");
     if (enable && !m->d_trace) {
-        CK_M(dalloc(m, &m->d_trace, (size_t)m->dplan.grid * m->dplan.nph * 2));
-        CK_M(cudaMemset(m->d_trace, 0, sizeof(unsigned long long) * m->dplan.grid * m->dplan.nph * 2));
+        CK_M(dalloc(m, &m->d_trace, (size_t)m->dplan.grid * m->dplan.nph * 4));
+        CK_M(cudaMemset(m->d_trace, 0, sizeof(unsigned long long) * m->dplan.grid * m->dplan.nph * 4));
     }
     if ((bool)enable != m->trace) {
         m->trace = enable != 0;
@@ -1706,7 +1707,7 @@ ACM_API int acm_model_trace(acm_model *m, int32_t enable) {
 
 ACM_API int acm_model_trace_read(acm_model *m, uint64_t *out, int64_t cap, int32_t *nblocks, int32_t *nphases) {
     if (!m || !m->trace || !m->d_trace || !out) return set_err(m, ACM_ERR_INVALID, "tracing not enabled");
-    const int64_t n = (int64_t)m->dplan.grid * m->dplan.nph * 2;
+    const int64_t n = (int64_t)m->dplan.grid * m->dplan.nph * 4;
     if (cap < n) return set_err(m, ACM_ERR_INVALID, "trace buffer too small");
     cudaSetDevice(m->e->device);
     CK_M(cudaMemcpy(out, m->d_trace, sizeof(uint64_t) * n, cudaMemcpyDeviceToHost));

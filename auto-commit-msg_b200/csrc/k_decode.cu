@@ -27,6 +27,7 @@
 
 #include "attn_dev.cuh"
 #include "common.cuh"
+#include "gemv1.cuh"
 #include "gemv_dev.cuh"
 #include "kernels.h"
 #include "quant.cuh"
@@ -34,8 +35,8 @@
 namespace acm {
 
 constexpr int DCH = DEC_CHUNK;  // attention chunk (positions)
-constexpr int DGROUPS = 4;    // attention groups per CTA (4 warps each)
-constexpr int DNCW = 16;      // consumer warps
+constexpr int DGROUPS = 3;    // attention groups per CTA (4 warps each)
+constexpr int DNCW = 15;      // consumer warps (16 warps in all: 128 registers a thread)
 constexpr int DNT = DNCW * 32 + 32;
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
@@ -52,6 +53,8 @@ __device__ __forceinline__ unsigned long long gtimer() {
 
 // Grid barrier among the consumer warps of all CTAs; bounded wait.  With a
 // trace buffer, records when this CTA arrives (slot arrive) and leaves.
+// Trace slots per (CTA, phase): 0 barrier left (phase start), 1 activations
+// staged, 2 first weights stage ready, 3 barrier arrival (phase end).
 __device__ __forceinline__ bool grid_sync(unsigned *bar, unsigned target, int *abort_flag,
                                           unsigned long long *arrive = nullptr, unsigned long long *leave = nullptr) {
     named_sync(1, DNCW * 32);
@@ -91,6 +94,7 @@ struct AttnMetaGroup {
 template <int HD>
 __device__ void attn_phase(const DecArgs &A, const DecPhase &P, float *area, AttnMetaGroup *meta) {
     const int tid = threadIdx.x, grp = tid >> 7, gtid = tid & 127, bid = 2 + grp;
+    if (grp >= DGROUPS) return;  // the last consumer warps sit attention out
     const int nkv = A.a.n_head_kv;
     float *sm = area + grp * A.attn_group_floats;
     AttnMetaGroup &mg = meta[grp];
@@ -132,36 +136,48 @@ __device__ void attn_phase(const DecArgs &A, const DecPhase &P, float *area, Att
     if (P.layer == 0 && gtid == 0) mg.n = k;
 }
 
+// A GEMV phase: the activations staged once (RMSNorm-ed when the phase has a
+// norm weight) and held in registers, the rows consumed from the ring by warp
+// teams (gemv1_ring); the lm_head phase (lanes per row: P.lpr) keeps the wide
+// span decoder.  Returns false on abort.
 template <int T>
-__device__ __forceinline__ void gemv_phase(const DecArgs &A, const DecPhase &P, uint64_t *full, uint64_t *empty,
-                                           const uint8_t *stg, float *area, uint32_t cur) {
-    GemvArgs a{};
-    a.nseg = 1;
-    a.x = P.x;
-    a.ldx = P.ldx;
-    a.k = P.k;
-    a.m = A.ntok;
-    a.norm_w = P.norm_w;
-    a.eps = A.eps;
-    a.ns = A.ns;
-    a.stage_bytes = A.sb;
-    a.lpr = P.lpr;
-    float *xs = area;
-    float *xsum = xs + x_area_floats(P.k, 1, P.lpr);
-    float *red = xsum + 2 * (P.k / 32);
-    prep_x<T, 1>(a, xs, xsum, red);
-    if (P.lpr) consume_wide<T, 1>(a, P.seg, P.r0, P.r1, full, empty, stg, xs, xsum, cur);
-    else consume_unit<T, 1>(a, P.seg, P.r0, P.r1, full, empty, stg, xs, reinterpret_cast<const float2 *>(xsum), cur);
+__device__ __forceinline__ bool gemv_phase(const DecArgs &A, const DecPhase &P, uint64_t *full, uint64_t *empty,
+                                           const uint8_t *stg, float *area, uint32_t cur, XStage &xst,
+                                           int *abort_flag, unsigned long long *tp) {
+    if (P.lpr) {
+        GemvArgs a{};
+        a.nseg = 1;
+        a.x = P.x;
+        a.ldx = P.ldx;
+        a.k = P.k;
+        a.m = A.ntok;
+        a.norm_w = P.norm_w;
+        a.eps = A.eps;
+        a.ns = A.ns;
+        a.stage_bytes = A.sb;
+        a.lpr = P.lpr;
+        float *xs = area;
+        float *xsum = xs + x_area_floats(P.k, 1, P.lpr);
+        float *red = xsum + 2 * (P.k / 32);
+        prep_x<T, 1, DNCW>(a, xs, xsum, red);
+        consume_wide<T, 1, DNCW>(a, P.seg, P.r0, P.r1, full, empty, stg, xs, xsum, cur);
+        return true;
+    }
+    float *xs = area, *red = xs + P.k, *part = red + 32;
+    stage_x<T>(P.x, P.norm_w, P.k, A.eps, xs, red, xst, DNCW * 32, 1);
+    if (tp && threadIdx.x == 0) tp[1] = gtimer();
+    return gemv1_ring<T>(P.seg, P.r0, P.r1, P.k, full, empty, stg, A.ns, A.sb, cur, xs, part, A.part_rows, DNCW,
+                         abort_flag, tp);
 }
 
 template <int T, int... Ts>
-__device__ __forceinline__ void gemv_dispatch(int type, const DecArgs &A, const DecPhase &P, uint64_t *full,
-                                              uint64_t *empty, const uint8_t *stg, float *area, uint32_t cur) {
-    if (type == T) {
-        gemv_phase<T>(A, P, full, empty, stg, area, cur);
-        return;
-    }
-    if constexpr (sizeof...(Ts) > 0) gemv_dispatch<Ts...>(type, A, P, full, empty, stg, area, cur);
+__device__ __forceinline__ bool gemv_dispatch(int type, const DecArgs &A, const DecPhase &P, uint64_t *full,
+                                              uint64_t *empty, const uint8_t *stg, float *area, uint32_t cur,
+                                              XStage &xst, int *abort_flag, unsigned long long *tp) {
+    if (type == T) return gemv_phase<T>(A, P, full, empty, stg, area, cur, xst, abort_flag, tp);
+    if constexpr (sizeof...(Ts) > 0)
+        return gemv_dispatch<Ts...>(type, A, P, full, empty, stg, area, cur, xst, abort_flag, tp);
+    return true;
 }
 
 template <int HD, int... Ts>
@@ -224,16 +240,21 @@ __global__ void __launch_bounds__(DNT, 1) k_decode(const __grid_constant__ DecAr
         return;
     }
     uint32_t cur = 0;
-    unsigned long long *tr = A.trace ? A.trace + (size_t)blockIdx.x * A.nph * 2 : nullptr;
+    unsigned long long *tr = A.trace ? A.trace + (size_t)blockIdx.x * A.nph * 4 : nullptr;
     if (tr && tid == 0) tr[0] = gtimer();
     for (int p = 0; p < A.nph; p++) {
-        if (p > 0 && !grid_sync(A.bar, (unsigned)p * gridDim.x, abort_flag, tr ? tr + 2 * (p - 1) + 1 : nullptr,
-                                tr ? tr + 2 * p : nullptr))
-            return;
         const DecPhase &P = ph[p];
+        XStage xst;
+        // the phase's norm weights never change: load them before the barrier
+        if (P.kind == DPH_GEMV && !P.lpr) stage_x_pre(P.norm_w, P.k, xst, DNCW * 32);
+        if (p > 0 && !grid_sync(A.bar, (unsigned)p * gridDim.x, abort_flag, tr ? tr + 4 * (p - 1) + 3 : nullptr,
+                                tr ? tr + 4 * p : nullptr))
+            return;
         if (P.kind == DPH_GEMV) {
             if (P.r1 > P.r0) {
-                gemv_dispatch<Ts...>(P.seg.type, A, P, full, empty, stg, area, cur);
+                if (!gemv_dispatch<Ts...>(P.seg.type, A, P, full, empty, stg, area, cur, xst, abort_flag,
+                                          tr ? tr + 4 * p : nullptr))
+                    return;
                 const int R = P.seg.rows_per_stage;
                 cur += (uint32_t)((P.r1 - P.r0 + R - 1) / R);
             }
@@ -244,11 +265,11 @@ __global__ void __launch_bounds__(DNT, 1) k_decode(const __grid_constant__ DecAr
     if (A.amax == nullptr) {
         if (tr) {
             named_sync(1, DNCW * 32);
-            if (tid == 0) tr[2 * (A.nph - 1) + 1] = gtimer();
+            if (tid == 0) tr[4 * (A.nph - 1) + 3] = gtimer();
         }
         return;
     }
-    if (!grid_sync(A.bar, (unsigned)A.nph * gridDim.x, abort_flag, tr ? tr + 2 * (A.nph - 1) + 1 : nullptr)) return;
+    if (!grid_sync(A.bar, (unsigned)A.nph * gridDim.x, abort_flag, tr ? tr + 4 * (A.nph - 1) + 3 : nullptr)) return;
     if (blockIdx.x == 0 && tid < A.ntok) {
         // greedy: the argmax keys of the lm_head phase -> next input token
         const int t = tid;
@@ -413,7 +434,19 @@ bool decode_plan(DecPlan &plan, const DecLayerDesc *layers, int n_layers, const 
             while (lpr * 2 <= 4 && nsb % (lpr * 2) == 0) lpr *= 2;
         }
         P.lpr = lpr;
-        area = std::max(area, x_bytes(P.k, 1, lpr) - 128);
+        if (lpr) {
+            area = std::max(area, x_bytes(P.k, 1, lpr) - 128);
+        } else {
+            // staged activations + 32 floats of scratch + team partial sums
+            for (const Seg &sgi : sg) {
+                const int ts = row_geo(sgi.d.type, P.k).ts, nt = DNCW / ts;
+                if (nt < 1) return false;
+                const int64_t rmax = (plan.sb - 64) / (row_bytes(sgi.d.type, P.k) * (sgi.d.w2 ? 2 : 1));
+                const int prow = ts > 1 ? (int)((rmax + nt - 1) / nt) : 1;
+                plan.part_rows = std::max(plan.part_rows, prow);
+                area = std::max(area, ((size_t)P.k + 32 + (size_t)nt * (prow * 2 * ts + ts)) * 4);
+            }
+        }
         int cta0 = 0;
         for (size_t i = 0; i < sg.size(); i++) {
             int nc = (int)((double)sg[i].rb * sg[i].d.n / total * grid + 0.5);

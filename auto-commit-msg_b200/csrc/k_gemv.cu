@@ -35,7 +35,7 @@
 namespace acm {
 
 __device__ int g_dev_error = 0;  // declared in common.cuh (relocatable device code)
-__device__ uint32_t g_wait_limit = WAIT_LIMIT;
+__constant__ uint32_t g_wait_limit = WAIT_LIMIT;
 bool g_pdl = [] {
     const char *e = getenv("ACM_PDL");
     return !(e && e[0] == '0');
@@ -302,22 +302,20 @@ static cudaError_t gemv_launch_group(const GemvSegDesc *segs, int nseg, int ta, 
     }
 }
 
-static bool gemv1_on() {
-    static const bool on = [] {
-        const char *e = getenv("ACM_GEMV1");
-        return e && e[0] == '1';
-    }();
-    return on;
-}
-
 cudaError_t gemv_launch(const GemvSegDesc *segs, int nseg, const float *x, int ldx, int64_t k, int m,
                         const float *norm_w, float eps, int num_sms, cudaStream_t st, const L2Range *pf, int npf) {
     if (nseg < 1 || nseg > GEMV_MAX_SEG || m < 1 || m > 8) return cudaErrorInvalidValue;
-    if (m == 1 && gemv1_on() && !((uintptr_t)x & 15) && !(norm_w && ((uintptr_t)norm_w & 15))) {
-        // one token: the batch-1 kernel (activations in registers, lean CTAs)
+    if (m == 1 && !((uintptr_t)x & 15) && !(norm_w && ((uintptr_t)norm_w & 15))) {
+        // one token: the batch-1 kernel (activations in registers); matrices
+        // of more than ~128 rows per SM (lm_head) stay on the wide path below,
+        // whose lanes own whole super-blocks
         bool ok = true;
-        for (int i = 0; i < nseg; i++) ok &= gemv1_supported(segs[i].type, k);
-        if (ok) return gemv1_launch(segs, nseg, x, k, norm_w, eps, num_sms, st);
+        int64_t rows = 0;
+        for (int i = 0; i < nseg; i++) {
+            ok &= gemv1_supported(segs[i].type, k);
+            rows += segs[i].n;
+        }
+        if (ok && rows < 128 * (int64_t)num_sms) return gemv1_launch(segs, nseg, x, k, norm_w, eps, num_sms, st, pf, npf);
     }
     // common instance: every type equal, or exactly {Q4_K, Q6_K}
     bool same = true, q46 = true;

@@ -21,20 +21,15 @@
 
 namespace acm {
 
-// 16 warps (whole teams) per CTA: more than 64 registers a thread, so one CTA
-// per SM -- the block scheduler then spreads the 148 CTAs over all SMs (CTAs
-// that could share an SM were packed onto a third of them).
-template <int TA, int TB>
-__global__ void __launch_bounds__(512, 1) k_gemv1(const __grid_constant__ Gemv1Args a) {
-    extern __shared__ __align__(128) uint8_t smem[];
+// The CTA's matvec in format T: team geometry, the weight copies and the L2
+// prefetch before the dependency wait, then the activations and the rows.
+template <int T>
+__device__ __forceinline__ void gemv1_cta(const Gemv1Args &a, const GemvSeg &s, uint8_t *smem) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int TS = a.ts, NT = (int)(blockDim.x >> 5) / TS;
+    const RowGeo geo = row_geo(T, a.k);
+    const int TS = geo.ts, NT = (int)(blockDim.x >> 5) / TS;
     const int team = warp / TS, tw = warp - team * TS;
-    int sid = 0;
-#pragma unroll 1
-    for (int i = 1; i < a.nseg; i++)
-        if ((int)blockIdx.x >= a.seg[i].cta0) sid = i;
-    const GemvSeg &s = a.seg[sid];
+    const bool active = team < NT;
     const int cta = (int)blockIdx.x - s.cta0;
     const int r0 = (int)((int64_t)s.n * cta / s.ncta), r1 = (int)((int64_t)s.n * (cta + 1) / s.ncta);
     const int n = r1 - r0;
@@ -44,7 +39,7 @@ __global__ void __launch_bounds__(512, 1) k_gemv1(const __grid_constant__ Gemv1A
     float *part = reinterpret_cast<float *>(smem + a.part_off) + (size_t)team * (a.part_rows * 2 * TS + TS);
     float *red = part + a.part_rows * 2 * TS;
     const int R = s.rows_per_stage;
-    const int nst = tr1 > tr0 ? (tr1 - tr0 + R - 1) / R : 0;
+    const int nst = (active && tr1 > tr0) ? (tr1 - tr0 + R - 1) / R : 0;
     trace_stamp(a.trace, 0);
     if (a.trace && threadIdx.x == 0) {
         uint32_t smid;
@@ -58,24 +53,45 @@ __global__ void __launch_bounds__(512, 1) k_gemv1(const __grid_constant__ Gemv1A
         // weights do not depend on earlier kernels: stream them before the wait
         for (int i = 0; i < min(nst, a.nstage); i++) gemv1_issue(a, s, tr0, tr1, i, bar, wbuf);
     }
+    if (threadIdx.x == 32) {
+        // this CTA's share of the next matvecs' weights into L2
+        for (int i = 0; i < a.npf; i++) {
+            const int64_t bytes = a.pf[i].bytes;
+            const int64_t chunk = ((bytes + gridDim.x - 1) / gridDim.x + 15) & ~int64_t(15);
+            const int64_t off = (int64_t)blockIdx.x * chunk;
+            if (off >= bytes) continue;
+            const int64_t len = std::min<int64_t>(chunk, bytes - off) & ~int64_t(15);
+            if (len > 0) prefetch_l2(static_cast<const uint8_t *>(a.pf[i].p) + off, (uint32_t)len);
+        }
+    }
     XStage xst;
-    stage_x_pre(a.norm_w, a.k, xst);
+    stage_x_pre(a.norm_w, a.k, xst, blockDim.x);
     trace_stamp(a.trace, 1);
     pdl_trigger();
     pdl_wait();
     trace_stamp(a.trace, 2);
     float *xs = reinterpret_cast<float *>(smem + GEMV1_BAR_BYTES);
-    float *xred = xs + a.k;
+    // every thread takes part (its barriers also order the mbarrier inits)
+    stage_x<T>(a.x, a.norm_w, a.k, a.eps, xs, xs + a.k, xst, blockDim.x, 0);
+    trace_stamp(a.trace, 3);
+    if (nst > 0) gemv1_rows<T>(a, s, geo, tr0, tr1, bar, wbuf, nst, tw, 1 + team, part, red, xs);
+}
+
+// 16 warps per CTA, more than 64 registers a thread: one CTA per SM, and the
+// block scheduler spreads the 148 CTAs over all SMs (CTAs that could share
+// an SM were packed onto a third of them).
+template <int TA, int TB>
+__global__ void __launch_bounds__(512, 1) k_gemv1(const __grid_constant__ Gemv1Args a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    int sid = 0;
+#pragma unroll 1
+    for (int i = 1; i < a.nseg; i++)
+        if ((int)blockIdx.x >= a.seg[i].cta0) sid = i;
+    const GemvSeg &s = a.seg[sid];
     if (s.type == TA) {
-        stage_x<TA>(a.x, a.norm_w, a.k, a.eps, xs, xred, xst);  // also orders the barrier inits for every warp
-        trace_stamp(a.trace, 3);
-        if (nst > 0) gemv1_rows<TA>(a, s, tr0, tr1, bar, wbuf, nst, tw, 1 + team, part, red, xs);
+        gemv1_cta<TA>(a, s, smem);
     } else if constexpr (TB != TA) {
-        if (s.type == TB) {
-            stage_x<TB>(a.x, a.norm_w, a.k, a.eps, xs, xred, xst);
-            trace_stamp(a.trace, 3);
-            if (nst > 0) gemv1_rows<TB>(a, s, tr0, tr1, bar, wbuf, nst, tw, 1 + team, part, red, xs);
-        }
+        if (s.type == TB) gemv1_cta<TB>(a, s, smem);
     }
 }
 
@@ -97,7 +113,8 @@ int gemv1_trace_used() { return g_trace_next; }
 static const int SMALL_SMEM = 128 * 1024;
 
 bool gemv1_supported(int type, int64_t k) {
-    return type_ok(type) && k >= 32 && k % 32 == 0 && k % blk_elems(type) == 0 && k <= 1024 * GEMV1_MAX_TS;
+    return type_ok(type) && k >= 32 && k % 32 == 0 && k % blk_elems(type) == 0 && k % lane_elems_rt(type) == 0 &&
+           row_geo(type, (int)k).ts <= GEMV1_MAX_TS;
 }
 
 template <int TA, int TB>
@@ -158,34 +175,39 @@ static void split_ctas1(const GemvSegDesc *segs, int nseg, int64_t k, int num_sm
 
 // One launch for matrices whose types are {ta} or {ta, tb}.
 static cudaError_t gemv1_group(const GemvSegDesc *segs, int nseg, int ta, int tb, const float *x, int64_t k,
-                               const float *norm_w, float eps, int num_sms, cudaStream_t st) {
-    const int U = (int)(k / 32), TS = (U + 31) / 32;
-    if (TS > GEMV1_MAX_TS) return cudaErrorInvalidValue;
+                               const float *norm_w, float eps, int num_sms, cudaStream_t st, const L2Range *pf,
+                               int npf) {
+    // teams per segment format: 16 warps, teams of row_geo().ts warps
+    int tsmax = 1, ntc[GEMV_MAX_SEG];
+    for (int i = 0; i < nseg; i++) {
+        const int ts = row_geo(segs[i].type, (int)k).ts;
+        if (ts > GEMV1_MAX_TS) return cudaErrorInvalidValue;
+        tsmax = std::max(tsmax, ts);
+        ntc[i] = 16 / ts;
+    }
     int nc[GEMV_MAX_SEG];
     split_ctas1(segs, nseg, k, num_sms, nc);
     int64_t maxrow = 0;
     for (int i = 0; i < nseg; i++) maxrow = std::max(maxrow, row_bytes(segs[i].type, k) * (segs[i].w2 ? 2 : 1));
-    // bytes of the largest per-team row range for a team count
-    auto team_need = [&](int nt) {
-        int64_t need = 0;
-        for (int i = 0; i < nseg; i++) {
-            const int64_t rows_cta = (segs[i].n + nc[i] - 1) / nc[i];
-            const int64_t rows_t = (rows_cta + nt - 1) / nt;
-            need = std::max(need, rows_t * row_bytes(segs[i].type, k) * (segs[i].w2 ? 2 : 1));
-        }
-        return need + 64;  // 16-byte rounding of up to two copies + the word loader's over-read
-    };
-    // small matrices: 8 warps (whole teams), every team's rows in one stage
+    // bytes of the largest per-team row range
+    int64_t need = 0;
+    for (int i = 0; i < nseg; i++) {
+        const int64_t rows_cta = (segs[i].n + nc[i] - 1) / nc[i];
+        const int64_t rows_t = (rows_cta + ntc[i] - 1) / ntc[i];
+        need = std::max(need, rows_t * row_bytes(segs[i].type, k) * (segs[i].w2 ? 2 : 1));
+    }
+    need += 64;  // 16-byte rounding of up to two copies + the word loader's over-read
     // shared layout: [mbarriers][x: K floats + 32 of scratch][stages][team partials]
     const int xb = (int)(((k + 32) * 4 + 127) / 128 * 128);
-    const int nt = std::max(1, 16 / TS);
+    int nt = 1;  // stage slots: one per team of the format with the most teams
+    for (int i = 0; i < nseg; i++) nt = std::max(nt, ntc[i]);
     int nstage = 1;
-    int64_t sb = (team_need(nt) + 127) / 128 * 128;
+    int64_t sb = (need + 127) / 128 * 128;
     const int64_t part_cap = 64;  // rows per stage of a multi-warp team
-    const int64_t part_bytes = TS > 1 ? (int64_t)nt * (part_cap * 2 * TS + TS) * 4 : 0;
+    const int64_t part_bytes = tsmax > 1 ? (int64_t)nt * (part_cap * 2 * tsmax + tsmax) * 4 : 0;
     const int64_t room = SMEM_MAX1 - GEMV1_BAR_BYTES - xb - part_bytes;
     if ((int64_t)nt * sb > std::min<int64_t>(room, SMALL_SMEM)) {
-        // large matrices (lm_head): each team double-buffers its rows
+        // large matrices: each team double-buffers its rows
         nstage = 2;
         sb = std::min<int64_t>(sb, (room / (nt * nstage)) & ~int64_t(127));
         if (sb < maxrow + 64) return cudaErrorInvalidValue;
@@ -196,10 +218,12 @@ static cudaError_t gemv1_group(const GemvSegDesc *segs, int nseg, int ta, int tb
     a.k = (int)k;
     a.norm_w = norm_w;
     a.eps = eps;
-    a.ts = TS;
     a.nstage = nstage;
     a.stage_bytes = (int)sb;
     a.trace = nullptr;
+    a.npf = 0;
+    for (int i = 0; i < npf && a.npf < GEMV_MAX_PF; i++)
+        if (pf[i].p && pf[i].bytes >= 16 && ((uintptr_t)pf[i].p & 15) == 0) a.pf[a.npf++] = pf[i];
     if (g_trace_buf && g_trace_next < g_trace_slots)
         a.trace = g_trace_buf + (size_t)(g_trace_next++) * GEMV1_TRACE_CTAS * 8;
     int grid = 0, part_rows = 1;
@@ -222,7 +246,7 @@ static cudaError_t gemv1_group(const GemvSegDesc *segs, int nseg, int ta, int tb
         g.cta0 = grid;
         grid += nc[i];
         int64_t rps = (sb - 64) / (g.rb + g.rb2);
-        if (TS > 1) rps = std::min(rps, part_cap);
+        if (tsmax > 1) rps = std::min(rps, part_cap);
         g.rows_per_stage = (int)rps;
         if (g.rows_per_stage < 1) return cudaErrorInvalidValue;
         part_rows = std::max(part_rows, g.rows_per_stage);
@@ -230,13 +254,13 @@ static cudaError_t gemv1_group(const GemvSegDesc *segs, int nseg, int ta, int tb
     a.part_rows = part_rows;
     a.stage_off = GEMV1_BAR_BYTES + xb;
     a.part_off = (int)(a.stage_off + (size_t)nt * nstage * sb);
-    const size_t smem = (size_t)a.part_off + (TS > 1 ? (size_t)nt * (part_rows * 2 * TS + TS) * 4 : 0);
+    const size_t smem = (size_t)a.part_off + (tsmax > 1 ? (size_t)nt * (part_rows * 2 * tsmax + tsmax) * 4 : 0);
     if (smem > (size_t)SMEM_MAX1) return cudaErrorInvalidValue;
-    return launch_types1(a, ta, tb, grid, nt * TS * 32, smem, st);
+    return launch_types1(a, ta, tb, grid, 512, smem, st);
 }
 
 cudaError_t gemv1_launch(const GemvSegDesc *segs, int nseg, const float *x, int64_t k, const float *norm_w,
-                         float eps, int num_sms, cudaStream_t st) {
+                         float eps, int num_sms, cudaStream_t st, const L2Range *pf, int npf) {
     if (nseg < 1 || nseg > GEMV_MAX_SEG || ((uintptr_t)x & 15) || (norm_w && ((uintptr_t)norm_w & 15)))
         return cudaErrorInvalidValue;
     bool same = true, q46 = true;
@@ -245,8 +269,8 @@ cudaError_t gemv1_launch(const GemvSegDesc *segs, int nseg, const float *x, int6
         same &= segs[i].type == segs[0].type;
         q46 &= segs[i].type == T_Q4_K || segs[i].type == T_Q6_K;
     }
-    if (same) return gemv1_group(segs, nseg, segs[0].type, segs[0].type, x, k, norm_w, eps, num_sms, st);
-    if (q46) return gemv1_group(segs, nseg, T_Q4_K, T_Q6_K, x, k, norm_w, eps, num_sms, st);
+    if (same) return gemv1_group(segs, nseg, segs[0].type, segs[0].type, x, k, norm_w, eps, num_sms, st, pf, npf);
+    if (q46) return gemv1_group(segs, nseg, T_Q4_K, T_Q6_K, x, k, norm_w, eps, num_sms, st, pf, npf);
     // otherwise one launch per distinct type (SMs split by bytes)
     double tot = 0;
     for (int j = 0; j < nseg; j++) tot += (double)row_bytes(segs[j].type, k) * segs[j].n;
@@ -263,7 +287,7 @@ cudaError_t gemv1_launch(const GemvSegDesc *segs, int nseg, const float *x, int6
             }
         const int sms = std::max(1, (int)(num_sms * frac / tot + 0.5));
         cudaError_t e = gemv1_group(grp.data(), (int)grp.size(), segs[i].type, segs[i].type, x, k, norm_w, eps, sms,
-                                    st);
+                                    st, pf, npf);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

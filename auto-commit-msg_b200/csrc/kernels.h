@@ -267,6 +267,7 @@ struct DecArgs {
     int nph, ntok;
     float eps;
     int ns, sb, ring_off, area_off, meta_off, attn_group_floats;
+    int part_rows;           // GEMV team partial rows per stage
     RopeDesc r;
     AttnDesc a;
     KVDesc kv;
@@ -299,6 +300,7 @@ struct DecLmDesc {
 };
 struct DecPlan {
     int inst = 0, grid = 0, nph = 0, ns = 0, sb = 0, ring_off = 0, area_off = 0, meta_off = 0, attn_group_floats = 0;
+    int part_rows = 1;
     size_t smem = 0;
     std::vector<DecPhase> table;
 };
@@ -318,7 +320,7 @@ constexpr uint32_t WAIT_LIMIT_DEFAULT = 1u << 22;
 // Batch-1 decode GEMV (k_gemv1.cu): activations in registers, lean CTAs.
 bool gemv1_supported(int type, int64_t k);
 cudaError_t gemv1_launch(const GemvSegDesc *segs, int nseg, const float *x, int64_t k, const float *norm_w,
-                         float eps, int num_sms, cudaStream_t st);
+                         float eps, int num_sms, cudaStream_t st, const L2Range *pf = nullptr, int npf = 0);
 // Per-CTA timelines of batch-1 GEMV launches (profiling): launches planned
 // while buf is set take consecutive slots of 160 CTAs x 8 stamps; null: off.
 void gemv1_trace(unsigned long long *buf, int slots);

@@ -577,20 +577,27 @@ def run_profile(args):
         ids = m.Generate(prompt, acm.Sampler(0.0), args.tokens, stop_on_eos=False)
         print(f"decode {args.tokens} tokens: {args.tokens / m.Stats.Decode:.1f} tok/s", flush=True)
         if args.profile == "trace":
-            cap = 148 * 1024 * 2
+            cap = 148 * 1024 * 4
             buf = (C.c_uint64 * cap)()
             nb, nph = C.c_int32(), C.c_int32()
             if lib.acm_model_trace_read(m.handle, buf, cap, C.byref(nb), C.byref(nph)) == 0:
                 nb, nph = nb.value, nph.value
-                t = np.frombuffer(buf, dtype=np.uint64)[: nb * nph * 2].reshape(nb, nph, 2).astype(np.int64)
-                t -= t[:, 0, 0].min()
+                t = np.frombuffer(buf, dtype=np.uint64)[: nb * nph * 4].reshape(nb, nph, 4).astype(np.int64)
+                t0 = t[:, 0, 0].min()
                 kinds = ["qkv", "attn", "o", "ffn", "down"]
-                print(f"persistent kernel: {nb} CTAs, {nph} phases, token {t[:, -1, 1].max() / 1e3:.1f} us")
+                print(f"persistent kernel: {nb} CTAs, {nph} phases, token {(t[:, -1, 3].max() - t0) / 1e3:.1f} us")
                 for ki, kname in enumerate(kinds + ["lm_head"]):
                     ps = [nph - 1] if kname == "lm_head" else list(range(ki, nph - 1, 5))
-                    span = [(t[:, p, 1].max() - t[:, p, 0].min()) / 1e3 for p in ps]
-                    work = [float(np.median(t[:, p, 1] - t[:, p, 0])) / 1e3 for p in ps]
-                    print(f"  {kname:8s} phases {len(ps):3d}  span {np.mean(span):7.2f} us  median CTA work {np.mean(work):6.2f} us")
+                    span = [(t[:, p, 3].max() - t[:, p, 0].min()) / 1e3 for p in ps]
+                    work = [float(np.median(t[:, p, 3] - t[:, p, 0])) / 1e3 for p in ps]
+                    line = f"  {kname:8s} phases {len(ps):3d}  span {np.mean(span):7.2f} us  median CTA work {np.mean(work):6.2f} us"
+                    st = [p for p in ps if (t[:, p, 1] > 0).all()]
+                    if st:
+                        stage = np.mean([float(np.median(t[:, p, 1] - t[:, p, 0])) for p in st]) / 1e3
+                        wts = np.mean([float(np.median(t[:, p, 2] - t[:, p, 1])) for p in st if (t[:, p, 2] > 0).all()] or [0]) / 1e3
+                        rows = np.mean([float(np.median(t[:, p, 3] - np.maximum(t[:, p, 2], t[:, p, 1]))) for p in st]) / 1e3
+                        line += f"  (staged {stage:5.2f}, weights +{wts:5.2f}, rows {rows:5.2f})"
+                    print(line)
     m.close()
     eng.close()
 

@@ -258,8 +258,10 @@ ACM_API uint64_t acm_kernel_launches(void);
  * Stats wall clock, sampler.go:101-106): when enabled, batch-1 decode steps
  * on the persistent decode kernel record, per CTA and phase (q/k/v,
  * attention, o, gate/up, down per layer, then lm_head), the %globaltimer ns at
- * which the CTA started the phase and arrived at the following barrier.
- * acm_model_trace_read copies the last step's [nblocks][nphases][2] values. */
+ * which the CTA started the phase, had staged its activations and had its
+ * first weights stage (GEMV phases; 0 otherwise), and arrived at the
+ * following barrier.  acm_model_trace_read copies the last step's
+ * [nblocks][nphases][4] values. */
 ACM_API int acm_model_trace(acm_model *m, int32_t enable);
 ACM_API int acm_model_trace_read(acm_model *m, uint64_t *out, int64_t cap, int32_t *nblocks, int32_t *nphases);
 /* Tracing of the batch-1 decode GEMV launches, no reference counterpart:
