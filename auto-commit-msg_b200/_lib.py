@@ -85,6 +85,7 @@ SIGNATURES = {
     "acm_engine_stream": (P, [P]),
     "acm_engine_sync": (C.c_int, [P]),
     "acm_engine_set_kv_f16": (C.c_int, [P, C.c_int32]),
+    "acm_engine_set_wait_limit": (C.c_int, [P, C.c_int64]),
     "acm_model_last_timing": (C.c_int, [P, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "acm_kernel_launches": (C.c_uint64, []),
     "acm_model_bench_gemm": (C.c_int, [P, C.c_int32, C.c_int32, C.POINTER(C.c_double), C.POINTER(C.c_double),
@@ -92,6 +93,8 @@ SIGNATURES = {
     "acm_serve": (C.c_int, [P, C.POINTER(CRequest), C.c_int32, C.c_int32, C.c_int32, C.POINTER(CStats)]),
     "acm_model_trace": (C.c_int, [P, C.c_int32]),
     "acm_model_trace_read": (C.c_int, [P, P, C.c_int64, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
+    "acm_model_debug_layers": (C.c_int, [P, C.c_int32]),
+    "acm_model_debug_layers_read": (C.c_int, [P, P, C.c_int64]),
     "acm_model_trace_gemv": (C.c_int, [P, C.c_int32]),
     "acm_model_trace_gemv_read": (C.c_int, [P, P, C.c_int64, C.POINTER(C.c_int32)]),
     "acm_model_bench_gemv": (C.c_int, [P, C.c_int32, C.POINTER(C.c_double), C.POINTER(C.c_double),

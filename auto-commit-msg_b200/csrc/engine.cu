@@ -174,6 +174,8 @@ struct acm_model {
     unsigned *d_bar = nullptr;
     unsigned long long *d_trace = nullptr;  // phase timestamps of the persistent kernel (tracing on)
     unsigned long long *d_gtrace = nullptr; // per-CTA timelines of batch-1 GEMV launches (tracing on)
+    float *d_dbg = nullptr;                 // per-layer residual of the pass's last token (DebugLayer on)
+    bool dbg_layers = false;
     int gtrace_slots = 0, gtrace_on = 0;
     bool trace = false;
     int nchunks = 0;
@@ -554,6 +556,9 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
         } else {
             CK_M(gemm_launch({L.down->d, nullptr, (int)L.down->type, E, F, ntok, m->hb, F, m->x, E, EPI_ADD, nullptr, nullptr}, st));
         }
+        if (m->dbg_layers)  // DebugLayer (model.go:427-429): the residual after layer l, last token
+            CK_M(cudaMemcpyAsync(m->d_dbg + (size_t)l * E, m->x + (size_t)(ntok - 1) * E, sizeof(float) * E,
+                                 cudaMemcpyDeviceToDevice, st));
     }
     if (lm_count > 0) {
         // final RMSNorm + lm_head for the requested tokens, into their slots' logits rows
@@ -885,6 +890,15 @@ ACM_API int acm_engine_sync(acm_engine *e) {
 ACM_API int acm_engine_set_kv_f16(acm_engine *e, int32_t enable) {
     if (!e) return ACM_ERR_INVALID;
     e->kv_f16 = enable ? 1 : 0;
+    return ACM_OK;
+}
+
+ACM_API int acm_engine_set_wait_limit(acm_engine *e, int64_t polls) {
+    if (!e) return ACM_ERR_INVALID;
+    cudaSetDevice(e->device);
+    CK_E(cudaStreamSynchronize(e->stream));
+    const uint32_t v = polls < 0 ? WAIT_LIMIT_DEFAULT : (uint32_t)std::min<int64_t>(polls, 0xFFFFFFFFll);
+    CK_E(set_wait_limit(v));
     return ACM_OK;
 }
 
@@ -1713,6 +1727,32 @@ ACM_API int acm_model_trace_read(acm_model *m, uint64_t *out, int64_t cap, int32
     CK_M(cudaMemcpy(out, m->d_trace, sizeof(uint64_t) * n, cudaMemcpyDeviceToHost));
     if (nblocks) *nblocks = m->dplan.grid;
     if (nphases) *nphases = m->dplan.nph;
+    return ACM_OK;
+}
+
+ACM_API int acm_model_debug_layers(acm_model *m, int32_t enable) {
+    if (!m || !m->finalized) return set_err(m, ACM_ERR_INVALID, "model not finalized");
+    cudaSetDevice(m->e->device);
+    if (enable && !m->d_dbg) {
+        CK_M(dalloc(m, &m->d_dbg, (size_t)m->c.n_layers * m->c.n_embd));
+        CK_M(cudaMemset(m->d_dbg, 0, sizeof(float) * m->c.n_layers * m->c.n_embd));
+    }
+    if ((bool)enable != m->dbg_layers) {
+        m->dbg_layers = enable != 0;
+        // captured decode graphs hold (or lack) the copies: rebuild them
+        for (auto &g : m->graphs) cudaGraphExecDestroy(g.second.exec);
+        m->graphs.clear();
+    }
+    return ACM_OK;
+}
+
+ACM_API int acm_model_debug_layers_read(acm_model *m, float *out, int64_t cap) {
+    if (!m || !m->dbg_layers || !m->d_dbg || !out) return set_err(m, ACM_ERR_INVALID, "layer dumps not enabled");
+    const int64_t n = (int64_t)m->c.n_layers * m->c.n_embd;
+    if (cap < n) return set_err(m, ACM_ERR_INVALID, "buffer too small");
+    cudaSetDevice(m->e->device);
+    CK_M(cudaStreamSynchronize(m->e->stream));
+    CK_M(cudaMemcpy(out, m->d_dbg, sizeof(float) * n, cudaMemcpyDeviceToHost));
     return ACM_OK;
 }
 

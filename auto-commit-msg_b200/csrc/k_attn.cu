@@ -12,6 +12,7 @@
 // `nsplit` CTAs (flash-decoding); a second kernel merges the partial
 // (sum e*v, max, sum e) triples.
 #include <float.h>
+#include <stdlib.h>
 
 #include <algorithm>
 

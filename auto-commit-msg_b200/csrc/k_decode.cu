@@ -208,17 +208,20 @@ __global__ void __launch_bounds__(DNT, 1) k_decode(const __grid_constant__ DecAr
         // producer: stream this CTA's rows of every GEMV phase, in order
         if ((tid & 31) == 0) {
             uint32_t cur = 0;
-            for (int p = 0; p < A.nph; p++) {
+            bool stop = false;
+            for (int p = 0; p < A.nph && !stop; p++) {
                 const DecPhase &P = ph[p];
                 if (P.kind != DPH_GEMV || P.r1 <= P.r0) continue;
                 const GemvSeg &s = P.seg;
                 const int R = s.rows_per_stage, nst = (P.r1 - P.r0 + R - 1) / R;
                 for (int i = 0; i < nst; i++) {
-                    const uint32_t ring = cur + (uint32_t)i;
+                    const uint32_t ring = cur;  // stages issued so far
                     const int slot = (int)(ring % (uint32_t)A.ns);
                     if (ring >= (uint32_t)A.ns &&
-                        !mbar_wait(&empty[slot], ((ring / (uint32_t)A.ns) - 1u) & 1u))
-                        return;
+                        !mbar_wait(&empty[slot], ((ring / (uint32_t)A.ns) - 1u) & 1u)) {
+                        stop = true;
+                        break;
+                    }
                     const int ra = P.r0 + i * R, rbn = min(ra + R, P.r1);
                     const int64_t a0 = ((int64_t)ra * s.rb) & ~int64_t(15);
                     const int64_t a1 = ((int64_t)rbn * s.rb + 15) & ~int64_t(15);
@@ -233,9 +236,13 @@ __global__ void __launch_bounds__(DNT, 1) k_decode(const __grid_constant__ DecAr
                     mbar_arrive_expect_tx(&full[slot], total);
                     bulk_g2s(dst, s.w + a0, (uint32_t)(a1 - a0), &full[slot]);
                     if (s.w2) bulk_g2s(dst + (a1 - a0), s.w2 + c0, (uint32_t)(c1 - c0), &full[slot]);
+                    ++cur;
                 }
-                cur += (uint32_t)nst;
             }
+            // no copy may still be landing when the CTA exits: wait, with the
+            // fixed bound, for the last fill of every ring slot used
+            for (uint32_t r = cur > (uint32_t)A.ns ? cur - (uint32_t)A.ns : 0u; r < cur; r++)
+                mbar_wait_limit(&full[r % (uint32_t)A.ns], (r / (uint32_t)A.ns) & 1u, WAIT_LIMIT);
         }
         return;
     }

@@ -79,6 +79,7 @@ __global__ void __launch_bounds__(Cfg<MT>::NT, 1) k_gemv(const __grid_constant__
         // producer: weights do not depend on earlier kernels -- stream them
         // before waiting on the predecessor
         if ((tid & 31) == 0) {
+            int issued = 0;
             for (int i = 0; i < nst; i++) {
                 const int slot = i % NS;
                 if (i >= NS && !mbar_wait(&empty[slot], (uint32_t)(((i / NS) - 1) & 1))) break;
@@ -96,7 +97,13 @@ __global__ void __launch_bounds__(Cfg<MT>::NT, 1) k_gemv(const __grid_constant__
                 mbar_arrive_expect_tx(&full[slot], total);
                 bulk_g2s(dst, s.w + a0, (uint32_t)(a1 - a0), &full[slot]);
                 if (s.w2) bulk_g2s(dst + (a1 - a0), s.w2 + c0, (uint32_t)(c1 - c0), &full[slot]);
+                issued = i + 1;
             }
+            // no copy may still be landing when the CTA exits (the consumers
+            // leave early after a timed-out wait): wait, with the fixed bound,
+            // for the last fill of every stage used
+            for (int i = issued > NS ? issued - NS : 0; i < issued; i++)
+                mbar_wait_limit(&full[i % NS], (uint32_t)((i / NS) & 1), WAIT_LIMIT);
             // this CTA's share of the next matvec's weights into L2
             for (int i = 0; i < a.npf; i++) {
                 const int64_t bytes = a.pf[i].bytes;

@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_mma_gemm(const __grid_consta
         // for the last fill of every stage used
         for (int s = 0; s < MST && s < issued; s++) {
             const int last = s + ((issued - 1 - s) / MST) * MST;  // last kt that used stage s
-            mbar_wait(&full[s], (last / MST) & 1);
+            mbar_wait_limit(&full[s], (last / MST) & 1, WAIT_LIMIT);
         }
     } else if (warp == 1 && lane == 0) {
         // ---- MMA issuer ----
@@ -307,8 +307,8 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_mma_gemm(const __grid_consta
     __syncthreads();
     if (warp == 1) {
         // the accumulator must be idle before it is freed (immediate unless a
-        // wait above ran out)
-        mbar_wait(accf, 0);
+        // wait above ran out; the fixed bound, whatever the progress limit)
+        mbar_wait_limit(accf, 0, WAIT_LIMIT);
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
     }

@@ -242,6 +242,18 @@ class Model:
                                                _ptr(out), _ptr(lg)))
         return (out, lg) if want_logits else out
 
+    def DebugLayer(self, enable: bool = True) -> None:
+        """Turn the per-layer residual dump on or off (DebugLayer,
+        model.go:231-233, :427-429); see DebugLayers."""
+        self._check(_lib.lib().acm_model_debug_layers(self._h, 1 if enable else 0))
+
+    def DebugLayers(self) -> np.ndarray:
+        """Residual stream of the last pass's last token after each layer,
+        [n_layers][n_embd] (DebugLayer must be on)."""
+        out = np.zeros((self.Cfg.n_layers, self.Cfg.n_embd), dtype=np.float32)
+        self._check(_lib.lib().acm_model_debug_layers_read(self._h, _ptr(out), out.size))
+        return out
+
     def last_timing(self):
         a, b = C.c_double(), C.c_double()
         self._check(_lib.lib().acm_model_last_timing(self._h, C.byref(a), C.byref(b)))

@@ -102,6 +102,18 @@ ACM_API const char *acm_engine_error(acm_engine *e);
  * kernel (ACM_MEGA=1) is not used for such models.  Default: fp32. */
 ACM_API int acm_engine_set_kv_f16(acm_engine *e, int32_t enable);
 
+/* Failure detection, no reference counterpart.  Every device-side wait of
+ * the library's kernels (a weight stage landing, a pipeline slot freed) is
+ * bounded: after `polls` unsuccessful tests it records a timeout, lets the
+ * copies it started land, and returns, and the next call that synchronises
+ * reports ACM_ERR_TIMEOUT ("a device-side wait timed out") instead of
+ * hanging.  This sets the bound for the engine's device (polls < 0: the
+ * default, ~2^22 polls, seconds; 0: every wait that does not find its data
+ * already there gives up at once, which is how the tests make a wait run
+ * out).  It applies to kernels launched after the call, on every engine of
+ * that device. */
+ACM_API int acm_engine_set_wait_limit(acm_engine *e, int64_t polls);
+
 /* Create an empty model for `cfg`; replaces infer.Load's allocation part
  * (model.go:90-203).  max_seqs concurrent sequence slots, each up to
  * cfg->max_ctx positions. */
@@ -264,6 +276,17 @@ ACM_API uint64_t acm_kernel_launches(void);
  * [nblocks][nphases][4] values. */
 ACM_API int acm_model_trace(acm_model *m, int32_t enable);
 ACM_API int acm_model_trace_read(acm_model *m, uint64_t *out, int64_t cap, int32_t *nblocks, int32_t *nphases);
+/* DebugLayer (model.go:231-233, called at :427-429 after each layer's
+ * residual update): with enable != 0, every pass from now on (prefill chunks
+ * and decode steps; decode graphs are rebuilt) copies the residual stream x
+ * of its last token after each layer into a model buffer;
+ * acm_model_debug_layers_read copies the last pass's [n_layers][n_embd]
+ * values (after synchronising the model's stream).  The reference's hook
+ * sees all nTok rows and is a Go callback; here the device keeps the last
+ * row, the one the reference's layer_test.go inspects. */
+ACM_API int acm_model_debug_layers(acm_model *m, int32_t enable);
+ACM_API int acm_model_debug_layers_read(acm_model *m, float *out, int64_t cap);
+
 /* Tracing of the batch-1 decode GEMV launches, no reference counterpart:
  * with slots > 0, decode graphs are rebuilt so that each batch-1 GEMV launch
  * of a step takes one slot (in launch order) of 160 CTAs x 8 values: the

@@ -50,6 +50,8 @@ class Stats(C.Structure):
 
 
 _lib = None
+# DebugLayer callback: (layer, x, ntok, embd, ctx)
+_DEBUG_FN = C.CFUNCTYPE(None, C.c_int, C.POINTER(C.c_float), C.c_int, C.c_int, C.c_void_p)
 
 
 def lib():
@@ -87,6 +89,8 @@ def lib():
         L.or_model_config.argtypes = [P]
         L.or_model_config.restype = C.POINTER(Config)
         L.or_model_pos.argtypes = [P]
+        L.or_model_set_debug.argtypes = [P, _DEBUG_FN, C.c_void_p]
+        L.or_model_set_debug.restype = None
         L.or_model_reset.argtypes = [P]
         L.or_model_freqs.argtypes = [P]
         L.or_model_freqs.restype = C.POINTER(C.c_float)
@@ -206,6 +210,21 @@ class Model:
     def freqs(self) -> np.ndarray:
         p = lib().or_model_freqs(self.h)
         return np.ctypeslib.as_array(p, shape=(self.cfg.rope_dim // 2,)).copy()
+
+    def debug_layers(self, enable: bool = True) -> None:
+        """Record the residual stream of the last token after each layer
+        (the DebugLayer hook, model.go:427-429) on the following forwards."""
+        if not enable:
+            lib().or_model_set_debug(self.h, _DEBUG_FN(0), None)
+            self._dbg_cb = None
+            return
+        self.layers = np.zeros((self.cfg.n_layers, self.cfg.n_embd), dtype=np.float32)
+
+        def cb(li, x, ntok, embd, ctx):
+            row = np.ctypeslib.as_array(x, shape=(ntok * embd,))[(ntok - 1) * embd:]
+            self.layers[li] = row
+        self._dbg_cb = _DEBUG_FN(cb)
+        lib().or_model_set_debug(self.h, self._dbg_cb, None)
 
     def forward(self, tokens) -> np.ndarray:
         t = np.ascontiguousarray(tokens, dtype=np.int32)

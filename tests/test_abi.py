@@ -6,6 +6,8 @@ import os
 import re
 import struct
 
+import numpy as np
+
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -98,3 +100,16 @@ def test_parse_tensor_errors(acm, synth, tmp_path):
     p.write_bytes(oob + b"\0" * 64)
     with pytest.raises(acm.AcmError, match="tensor w: out of bounds"):
         acm.LoadConfig(str(p))
+
+
+def test_max_logit_first_max(acm):
+    """MaxLogit (model.go:462-471): the first of equal maxima wins; a host
+    function of the library, no device involved."""
+    rng = np.random.default_rng(3)
+    for n in (1, 7, 1000, 151936):
+        lg = rng.standard_normal(n).astype(np.float32)
+        assert acm.MaxLogit(lg) == int(np.argmax(lg))
+    lg = np.array([0.5, 2.0, -1.0, 2.0, 2.0], dtype=np.float32)
+    assert acm.MaxLogit(lg) == 1
+    lg = np.full(64, -3.0, dtype=np.float32)
+    assert acm.MaxLogit(lg) == 0
