@@ -315,7 +315,8 @@ cudaError_t gemv_launch(const GemvSegDesc *segs, int nseg, const float *x, int l
     if (m == 1 && !((uintptr_t)x & 15) && !(norm_w && ((uintptr_t)norm_w & 15))) {
         // one token: the batch-1 kernel (activations in registers); matrices
         // of more than ~128 rows per SM (lm_head) stay on the wide path below,
-        // whose lanes own whole super-blocks
+        // whose lanes own whole super-blocks (Q4_K 1024 x 151936: 34.9 us
+        // there, 49.8 us on the batch-1 kernel)
         bool ok = true;
         int64_t rows = 0;
         for (int i = 0; i < nseg; i++) {

@@ -77,9 +77,9 @@ __device__ __forceinline__ void gemv1_cta(const Gemv1Args &a, const GemvSeg &s, 
     if (nst > 0) gemv1_rows<T>(a, s, geo, tr0, tr1, bar, wbuf, nst, tw, 1 + team, part, red, xs);
 }
 
-// 16 warps per CTA, more than 64 registers a thread: one CTA per SM, and the
-// block scheduler spreads the 148 CTAs over all SMs (CTAs that could share
-// an SM were packed onto a third of them).
+// Up to 16 warps per CTA (12 in use, NWC), up to 128 registers a thread: one
+// CTA per SM, and the block scheduler spreads the 148 CTAs over all SMs (CTAs
+// that could share an SM were packed onto a third of them).
 template <int TA, int TB>
 __global__ void __launch_bounds__(512, 1) k_gemv1(const __grid_constant__ Gemv1Args a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -96,6 +96,7 @@ __global__ void __launch_bounds__(512, 1) k_gemv1(const __grid_constant__ Gemv1A
 }
 
 static const int SMEM_MAX1 = 227 * 1024;
+static const int NWC = 12;  // warps per CTA
 
 // Timeline tracing (profiling): launches planned while it is on take
 // consecutive slots of the buffer.
@@ -114,7 +115,7 @@ static const int SMALL_SMEM = 128 * 1024;
 
 bool gemv1_supported(int type, int64_t k) {
     return type_ok(type) && k >= 32 && k % 32 == 0 && k % blk_elems(type) == 0 && k % lane_elems_rt(type) == 0 &&
-           row_geo(type, (int)k).ts <= GEMV1_MAX_TS;
+           row_geo(type, (int)k).ts <= NWC;
 }
 
 template <int TA, int TB>
@@ -177,13 +178,17 @@ static void split_ctas1(const GemvSegDesc *segs, int nseg, int64_t k, int num_sm
 static cudaError_t gemv1_group(const GemvSegDesc *segs, int nseg, int ta, int tb, const float *x, int64_t k,
                                const float *norm_w, float eps, int num_sms, cudaStream_t st, const L2Range *pf,
                                int npf) {
-    // teams per segment format: 16 warps, teams of row_geo().ts warps
+    // teams per segment format: NWC warps, teams of row_geo().ts warps.  12
+    // warps of up to 128 registers: one GEMV CTA per SM (two would need more
+    // than the register file), with room left beside it for decode
+    // attention CTAs; measured 1070 tok/s against 1045 at 16 warps and 990
+    // at 8 (whose CTAs, two fitting per SM, were packed onto 106 SMs)
     int tsmax = 1, ntc[GEMV_MAX_SEG];
     for (int i = 0; i < nseg; i++) {
         const int ts = row_geo(segs[i].type, (int)k).ts;
-        if (ts > GEMV1_MAX_TS) return cudaErrorInvalidValue;
+        if (ts > GEMV1_MAX_TS || ts > NWC) return cudaErrorInvalidValue;
         tsmax = std::max(tsmax, ts);
-        ntc[i] = 16 / ts;
+        ntc[i] = NWC / ts;
     }
     int nc[GEMV_MAX_SEG];
     split_ctas1(segs, nseg, k, num_sms, nc);
@@ -256,7 +261,7 @@ static cudaError_t gemv1_group(const GemvSegDesc *segs, int nseg, int ta, int tb
     a.part_off = (int)(a.stage_off + (size_t)nt * nstage * sb);
     const size_t smem = (size_t)a.part_off + (tsmax > 1 ? (size_t)nt * (part_rows * 2 * tsmax + tsmax) * 4 : 0);
     if (smem > (size_t)SMEM_MAX1) return cudaErrorInvalidValue;
-    return launch_types1(a, ta, tb, grid, 512, smem, st);
+    return launch_types1(a, ta, tb, grid, NWC * 32, smem, st);
 }
 
 cudaError_t gemv1_launch(const GemvSegDesc *segs, int nseg, const float *x, int64_t k, const float *norm_w,
