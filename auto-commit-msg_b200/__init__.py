@@ -5,6 +5,8 @@ hand-written sm_100a kernels behind the C ABI of libacmcuda.so
 (include/acm.h).  The Python layer mirrors the reference's internal/infer API.
 """
 from ._lib import AcmError, Config, lib  # noqa: F401
-from .infer import Engine, Load, LoadConfig, MaxLogit, Model, Sampler, Stats  # noqa: F401
+from .infer import (Engine, Load, LoadBytes, LoadConfig, LoadConfigBytes, LoadMulti, MaxLogit, Model,  # noqa: F401
+                    Sampler, Stats)
 
-__all__ = ["AcmError", "Config", "Engine", "Load", "LoadConfig", "MaxLogit", "Model", "Sampler", "Stats", "lib"]
+__all__ = ["AcmError", "Config", "Engine", "Load", "LoadBytes", "LoadConfig", "LoadConfigBytes", "LoadMulti", "MaxLogit",
+           "Model", "Sampler", "Stats", "lib"]

@@ -65,6 +65,9 @@ SIGNATURES = {
     "acm_model_config": (C.c_int, [P, C.POINTER(Config)]),
     "acm_model_load_gguf": (C.c_int, [P, C.c_char_p, C.c_int32, C.c_int32, C.POINTER(P)]),
     "acm_load_config": (C.c_int, [C.c_char_p, C.c_int32, C.POINTER(Config), C.c_char_p, C.c_int32]),
+    "acm_model_load_gguf_mem": (C.c_int, [P, C.c_void_p, C.c_size_t, C.c_int32, C.c_int32, C.POINTER(P)]),
+    "acm_model_load_gguf_multi": (C.c_int, [C.POINTER(P), C.c_int32, C.c_char_p, C.c_int32, C.c_int32, C.POINTER(P)]),
+    "acm_load_config_mem": (C.c_int, [C.c_void_p, C.c_size_t, C.c_int32, C.POINTER(Config), C.c_char_p, C.c_int32]),
     "acm_seq_open": (C.c_int, [P, C.POINTER(C.c_int32)]),
     "acm_seq_close": (C.c_int, [P, C.c_int32]),
     "acm_seq_reset": (C.c_int, [P, C.c_int32]),

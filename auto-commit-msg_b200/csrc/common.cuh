@@ -118,6 +118,19 @@ __device__ __forceinline__ void cp_async_wait_group() {
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
+// Named barrier that also ANDs a predicate over its `nthreads` threads, so
+// that a group decides together (a bounded wait that gave up in one thread
+// must not leave the others at a later barrier).
+__device__ __forceinline__ bool named_and(int id, int nthreads, bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred a, b;\n\tsetp.ne.u32 a, %1, 0;\n\tbar.red.and.pred b, %2, %3, a;\n\t"
+        "selp.u32 %0, 1, 0, b;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)p), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -424,6 +424,33 @@ int attention_prefill_mma(acm_model *m, int layer, int seq, int pos0, int ntok) 
     return ACM_OK;
 }
 
+// Whether the in-kernel dequant tensor-core GEMM (k_mma_dq.cu) serves these
+// weights: every one a quantized GGUF type (one type, or Q4_K with Q6_K) and
+// K a multiple of 256.  No split cache is built for them.
+bool use_mma_dq(acm_model *m, std::initializer_list<DevTensor *> ts, int64_t k) {
+    if (k % 256 || !mma_ready(m)) return false;
+    int ta = -1, tb = -1;
+    for (DevTensor *t : ts) {
+        if (!t) continue;
+        const int ty = (int)t->type;
+        if (!dq_type(ty)) return false;
+        if (ta < 0) ta = ty;
+        else if (ty != ta) tb = ty;
+    }
+    if (tb >= 0 && !((ta == T_Q4_K && tb == T_Q6_K) || (ta == T_Q6_K && tb == T_Q4_K))) return false;
+    for (DevTensor *t : ts)
+        if (t && (int)t->type != ta && (int)t->type != tb) return false;
+    return true;
+}
+
+// Launch a tensor-core GEMM: weights dequantized in the kernel when the
+// segments carry GGUF rows (wtype >= 0), else from their split caches.
+cudaError_t mma_run(const MmaGemmSeg *segs, int nseg, const TensorMap *xh, const TensorMap *xl, int m, int k,
+                    cudaStream_t st, float *ws = nullptr, size_t wsf = 0) {
+    if (segs[0].wtype >= 0) return mma_dq_launch(segs, nseg, xh, xl, m, k, st, ws, wsf);
+    return mma_gemm_launch(segs, nseg, xh, xl, m, k, st, ws, wsf);
+}
+
 // Whether the tensor-core GEMM serves a GEMM of these weights (batches of
 // more than 8 tokens; exact split caches built here).
 bool use_mma(acm_model *m, std::initializer_list<DevTensor *> ts) {
@@ -462,14 +489,18 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
             // pay a DRAM round trip on the critical path)
             const L2Range pf_o[1] = {{L.o->d, (int64_t)L.o->nbytes}};
             CK_M(gemv_launch(sg, 3, m->x, E, E, ntok, L.attn_nw, eps, S, st, pf_o, 1));
-        } else if (use_mma(m, {L.q, L.k, L.v})) {
+        } else if (use_mma_dq(m, {L.q, L.k, L.v}, E) || use_mma(m, {L.q, L.k, L.v})) {
+            const bool dq = use_mma_dq(m, {L.q, L.k, L.v}, E);
             CK_M(rmsnorm_launch(m->x, E, L.attn_nw, m->h, E, ntok, E, eps, st));
             const TensorMap *xh, *xl;
             if (int rc = mma_split_x(m, m->h, E, ntok, E, &xh, &xl)) return rc;
-            MmaGemmSeg sg[3] = {{&L.q->mhi, &L.q->mlo, nullptr, nullptr, qd, EPI_STORE, m->q, qd, L.q_b, nullptr},
-                                {&L.k->mhi, &L.k->mlo, nullptr, nullptr, kvd, EPI_STORE, m->k, kvd, L.k_b, nullptr},
-                                {&L.v->mhi, &L.v->mlo, nullptr, nullptr, kvd, EPI_STORE, m->v, kvd, L.v_b, nullptr}};
-            CK_M(mma_gemm_launch(sg, 3, xh, xl, ntok, E, st));
+            MmaGemmSeg sg[3] = {{&L.q->mhi, &L.q->mlo, nullptr, nullptr, qd, EPI_STORE, m->q, qd, L.q_b, nullptr,
+                                 L.q->d, nullptr, dq ? (int)L.q->type : -1},
+                                {&L.k->mhi, &L.k->mlo, nullptr, nullptr, kvd, EPI_STORE, m->k, kvd, L.k_b, nullptr,
+                                 L.k->d, nullptr, dq ? (int)L.k->type : -1},
+                                {&L.v->mhi, &L.v->mlo, nullptr, nullptr, kvd, EPI_STORE, m->v, kvd, L.v_b, nullptr,
+                                 L.v->d, nullptr, dq ? (int)L.v->type : -1}};
+            CK_M(mma_run(sg, 3, xh, xl, ntok, E, st));
         } else {
             CK_M(rmsnorm_launch(m->x, E, L.attn_nw, m->h, E, ntok, E, eps, st));
             CK_M(gemm_launch({L.q->d, nullptr, (int)L.q->type, qd, E, ntok, m->h, E, m->q, qd, EPI_STORE, L.q_b, nullptr}, st));
@@ -497,11 +528,13 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
             GemvSegDesc so{L.o->d, nullptr, (int)L.o->type, E, EPI_ADD, m->x, E, nullptr, nullptr};
             const L2Range pf_f[2] = {{L.gate->d, (int64_t)L.gate->nbytes}, {L.up->d, (int64_t)L.up->nbytes}};
             CK_M(gemv_launch(&so, 1, m->att, qd, qd, ntok, nullptr, eps, S, st, pf_f, 2));
-        } else if (use_mma(m, {L.o})) {
+        } else if (use_mma_dq(m, {L.o}, qd) || use_mma(m, {L.o})) {
+            const bool dq = use_mma_dq(m, {L.o}, qd);
             const TensorMap *xh, *xl;
             if (int rc = mma_split_x(m, m->att, qd, ntok, qd, &xh, &xl)) return rc;
-            MmaGemmSeg so{&L.o->mhi, &L.o->mlo, nullptr, nullptr, E, EPI_ADD, m->x, E, nullptr, nullptr};
-            CK_M(mma_gemm_launch(&so, 1, xh, xl, ntok, qd, st, m->mma_ws, m->mma_ws_floats));
+            MmaGemmSeg so{&L.o->mhi, &L.o->mlo, nullptr, nullptr, E, EPI_ADD, m->x, E, nullptr, nullptr,
+                          L.o->d, nullptr, dq ? (int)L.o->type : -1};
+            CK_M(mma_run(&so, 1, xh, xl, ntok, qd, st, m->mma_ws, m->mma_ws_floats));
         } else {
             CK_M(gemm_launch({L.o->d, nullptr, (int)L.o->type, E, qd, ntok, m->att, qd, m->x, E, EPI_ADD, nullptr, nullptr}, st));
         }
@@ -518,13 +551,16 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
                 CK_M(gemv_launch(sf, 2, m->x, E, E, ntok, L.ffn_nw, eps, S, st));
                 CK_M(swiglu_launch(m->hb, m->hb2, m->hb, (int64_t)ntok * F, st));
             }
-        } else if (use_mma(m, {L.gate, L.up}) && F % 64 == 0) {
-            // both projections split to bf16: one paired launch whatever their types
+        } else if (F % 64 == 0 && ((pair && use_mma_dq(m, {L.gate, L.up}, E)) || use_mma(m, {L.gate, L.up}))) {
+            // one paired launch: both projections dequantized in the kernel
+            // (same type), else both split to bf16 whatever their types
+            const bool dq = pair && use_mma_dq(m, {L.gate, L.up}, E);
             CK_M(rmsnorm_launch(m->x, E, L.ffn_nw, m->h, E, ntok, E, eps, st));
             const TensorMap *xh, *xl;
             if (int rc = mma_split_x(m, m->h, E, ntok, E, &xh, &xl)) return rc;
-            MmaGemmSeg sf{&L.gate->mhi, &L.gate->mlo, &L.up->mhi, &L.up->mlo, F, EPI_SWIGLU, m->hb, F, nullptr, nullptr};
-            CK_M(mma_gemm_launch(&sf, 1, xh, xl, ntok, E, st));
+            MmaGemmSeg sf{&L.gate->mhi, &L.gate->mlo, &L.up->mhi, &L.up->mlo, F, EPI_SWIGLU, m->hb, F, nullptr, nullptr,
+                          L.gate->d, L.up->d, dq ? (int)L.gate->type : -1};
+            CK_M(mma_run(&sf, 1, xh, xl, ntok, E, st));
         } else {
             CK_M(rmsnorm_launch(m->x, E, L.ffn_nw, m->h, E, ntok, E, eps, st));
             if (pair) {
@@ -548,11 +584,13 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
                 npf = 3;
             }
             CK_M(gemv_launch(&sd, 1, m->hb, F, F, ntok, nullptr, eps, S, st, pf_n, npf));
-        } else if (use_mma(m, {L.down})) {
+        } else if (use_mma_dq(m, {L.down}, F) || use_mma(m, {L.down})) {
+            const bool dq = use_mma_dq(m, {L.down}, F);
             const TensorMap *xh, *xl;
             if (int rc = mma_split_x(m, m->hb, F, ntok, F, &xh, &xl)) return rc;
-            MmaGemmSeg sd{&L.down->mhi, &L.down->mlo, nullptr, nullptr, E, EPI_ADD, m->x, E, nullptr, nullptr};
-            CK_M(mma_gemm_launch(&sd, 1, xh, xl, ntok, F, st, m->mma_ws, m->mma_ws_floats));
+            MmaGemmSeg sd{&L.down->mhi, &L.down->mlo, nullptr, nullptr, E, EPI_ADD, m->x, E, nullptr, nullptr,
+                          L.down->d, nullptr, dq ? (int)L.down->type : -1};
+            CK_M(mma_run(&sd, 1, xh, xl, ntok, F, st, m->mma_ws, m->mma_ws_floats));
         } else {
             CK_M(gemm_launch({L.down->d, nullptr, (int)L.down->type, E, F, ntok, m->hb, F, m->x, E, EPI_ADD, nullptr, nullptr}, st));
         }
@@ -568,13 +606,14 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
             GemvSegDesc so{m->out->d, nullptr, (int)m->out->type, V, EPI_STORE, m->logits, c.vocab, nullptr,
                            m->d_seq + lm_first, amax};
             CK_M(gemv_launch(&so, 1, xin, E, E, lm_count, m->out_nw, eps, S, st));
-        } else if (use_mma(m, {m->out})) {
+        } else if (use_mma_dq(m, {m->out}, E) || use_mma(m, {m->out})) {
+            const bool dq = use_mma_dq(m, {m->out}, E);
             CK_M(rmsnorm_launch(xin, E, m->out_nw, m->h, E, lm_count, E, eps, st));
             const TensorMap *xh, *xl;
             if (int rc = mma_split_x(m, m->h, E, lm_count, E, &xh, &xl)) return rc;
             MmaGemmSeg sl{&m->out->mhi, &m->out->mlo, nullptr, nullptr, V, EPI_STORE, m->logits, c.vocab, nullptr,
-                          m->d_seq + lm_first};
-            CK_M(mma_gemm_launch(&sl, 1, xh, xl, lm_count, E, st));
+                          m->d_seq + lm_first, m->out->d, nullptr, dq ? (int)m->out->type : -1};
+            CK_M(mma_run(&sl, 1, xh, xl, lm_count, E, st));
         } else {
             CK_M(rmsnorm_launch(xin, E, m->out_nw, m->h, E, lm_count, E, eps, st));
             CK_M(gemm_launch({m->out->d, nullptr, (int)m->out->type, V, E, lm_count, m->h, E, m->logits, c.vocab,
@@ -946,86 +985,186 @@ int tensor_meta(acm_model *m, const char *name, uint32_t ggml_type, const uint64
     return ACM_OK;
 }
 
-// Upload of a whole GGUF (the fast path of acm_model_load_gguf): one device
-// arena for every used tensor (256-byte aligned slots, 64 zero bytes after
-// each), filled through two pinned staging buffers -- the host copies the
-// next chunk out of the mmap while the copy engine moves the previous one.
-int upload_gguf(acm_model *m, const gguf::File &f, const std::vector<const std::string *> &names) {
-    cudaStream_t st = m->e->stream;
-    std::vector<DevTensor> ts(names.size());
+// Upload of a whole GGUF (the fast path of acm_model_load_gguf) to n models,
+// one per engine (the same device may repeat): per model one device arena for
+// every used tensor (256-byte aligned slots, 64 zero bytes after each), filled
+// through two portable pinned staging buffers.  The host copies each chunk
+// out of the mapping ONCE and every device's copy engine takes it from the
+// same staging buffer, while the host fills the other buffer: the reference
+// maps the file once per process (app/model_unix.go:15-34), and a host that
+// drives several GPUs from one process reads it once for all of them.
+int upload_gguf(acm_model *const *ms, int n, const gguf::File &f, const std::vector<const std::string *> &names) {
+    std::vector<std::vector<DevTensor>> ts(n, std::vector<DevTensor>(names.size()));
     std::vector<size_t> offs(names.size());
+    std::vector<uint8_t *> arena(n, nullptr);
     size_t total = 0;
     for (size_t i = 0; i < names.size(); i++) {
         const gguf::Tensor &t = f.tensors.at(*names[i]);
-        if (int rc = tensor_meta(m, names[i]->c_str(), t.type, t.dims.data(), (int)t.dims.size(), t.nbytes, ts[i]))
-            return rc;
+        for (int d = 0; d < n; d++)
+            if (int rc = tensor_meta(ms[d], names[i]->c_str(), t.type, t.dims.data(), (int)t.dims.size(), t.nbytes,
+                                     ts[d][i]))
+                return rc;
         offs[i] = total;
         total += (t.nbytes + 64 + 255) & ~size_t(255);
     }
-    uint8_t *arena = nullptr;
-    CK_M(dalloc(m, &arena, total));
+    for (int d = 0; d < n; d++) {
+        acm_model *m = ms[d];
+        cudaSetDevice(m->e->device);
+        CK_M(dalloc(m, &arena[d], total));
+    }
     constexpr size_t CH = 64u << 20;
     uint8_t *stage[2] = {nullptr, nullptr};
-    cudaEvent_t done[2] = {nullptr, nullptr};
+    std::vector<cudaEvent_t> done(2 * (size_t)n, nullptr);  // [buffer][model]
     int rc = ACM_OK;
-    for (int b = 0; b < 2 && !rc; b++) {
-        if (cudaMallocHost(reinterpret_cast<void **>(&stage[b]), CH) != cudaSuccess ||
-            cudaEventCreateWithFlags(&done[b], cudaEventDisableTiming) != cudaSuccess)
-            rc = set_err(m, ACM_ERR_OOM, "pinned staging buffer");
+    for (int b = 0; b < 2 && !rc; b++)
+        if (cudaHostAlloc(reinterpret_cast<void **>(&stage[b]), CH, cudaHostAllocPortable) != cudaSuccess)
+            rc = set_err(ms[0], ACM_ERR_OOM, "pinned staging buffer");
+    for (int d = 0; d < n && !rc; d++) {
+        cudaSetDevice(ms[d]->e->device);
+        for (int b = 0; b < 2 && !rc; b++)
+            if (cudaEventCreateWithFlags(&done[(size_t)b * n + d], cudaEventDisableTiming) != cudaSuccess)
+                rc = set_err(ms[d], ACM_ERR_CUDA, "upload event");
     }
-    // the arena's bytes in order, CH at a time: tensor bytes from the mmap,
+    // the arena's bytes in order, CH at a time: tensor bytes from the mapping,
     // zeros for the padding after each tensor
     bool pending[2] = {false, false};
     size_t ti = 0;
     int b = 0;
     for (size_t pos = 0; pos < total && !rc; pos += CH) {
         if (pending[b]) {
-            cudaError_t e = cudaEventSynchronize(done[b]);  // staging buffer b free again
-            if (e != cudaSuccess) {
-                rc = set_err(m, ACM_ERR_CUDA, fmt("upload: %s", cudaGetErrorString(e)));
-                break;
+            // staging buffer b is free again once every device has copied it
+            for (int d = 0; d < n && !rc; d++) {
+                cudaError_t e = cudaEventSynchronize(done[(size_t)b * n + d]);
+                if (e != cudaSuccess) rc = set_err(ms[d], ACM_ERR_CUDA, fmt("upload: %s", cudaGetErrorString(e)));
             }
+            if (rc) break;
         }
-        const size_t n = std::min(CH, total - pos);
-        for (size_t q = 0; q < n;) {
+        const size_t len = std::min(CH, total - pos);
+        for (size_t q = 0; q < len;) {
             const size_t at = pos + q;
             while (ti + 1 < names.size() && offs[ti + 1] <= at) ti++;
             const gguf::Tensor &t = f.tensors.at(*names[ti]);
             const size_t end_t = offs[ti] + t.nbytes, end_slot = ti + 1 < names.size() ? offs[ti + 1] : total;
             if (at < end_t) {
-                const size_t c = std::min(end_t - at, n - q);
+                const size_t c = std::min(end_t - at, len - q);
                 memcpy(stage[b] + q, static_cast<const uint8_t *>(t.data) + (at - offs[ti]), c);
                 q += c;
             } else {
-                const size_t c = std::min(end_slot - at, n - q);
+                const size_t c = std::min(end_slot - at, len - q);
                 memset(stage[b] + q, 0, c);
                 q += c;
             }
         }
-        if (cudaMemcpyAsync(arena + pos, stage[b], n, cudaMemcpyHostToDevice, st) != cudaSuccess ||
-            cudaEventRecord(done[b], st) != cudaSuccess) {
-            rc = set_err(m, ACM_ERR_CUDA, "upload copy failed");
-            break;
+        for (int d = 0; d < n && !rc; d++) {
+            acm_model *m = ms[d];
+            cudaSetDevice(m->e->device);
+            if (cudaMemcpyAsync(arena[d] + pos, stage[b], len, cudaMemcpyHostToDevice, m->e->stream) != cudaSuccess ||
+                cudaEventRecord(done[(size_t)b * n + d], m->e->stream) != cudaSuccess)
+                rc = set_err(m, ACM_ERR_CUDA, "upload copy failed");
         }
         pending[b] = true;
         b ^= 1;
     }
-    if (!rc) {
-        cudaError_t e = cudaStreamSynchronize(st);
-        if (e != cudaSuccess) rc = set_err(m, ACM_ERR_CUDA, fmt("upload: %s", cudaGetErrorString(e)));
-    } else {
-        cudaStreamSynchronize(st);  // no copy may still read a staging buffer
+    // no copy may still read a staging buffer when it is freed
+    for (int d = 0; d < n; d++) {
+        acm_model *m = ms[d];
+        cudaSetDevice(m->e->device);
+        cudaError_t e = cudaStreamSynchronize(m->e->stream);
+        if (!rc && e != cudaSuccess) rc = set_err(m, ACM_ERR_CUDA, fmt("upload: %s", cudaGetErrorString(e)));
     }
-    for (int k = 0; k < 2; k++) {
-        if (done[k]) cudaEventDestroy(done[k]);
+    for (cudaEvent_t ev : done)
+        if (ev) cudaEventDestroy(ev);
+    for (int k = 0; k < 2; k++)
         if (stage[k]) cudaFreeHost(stage[k]);
-    }
     if (rc) return rc;
-    for (size_t i = 0; i < names.size(); i++) {
-        ts[i].d = arena + offs[i];
-        m->tensors[*names[i]] = std::move(ts[i]);
-    }
+    for (int d = 0; d < n; d++)
+        for (size_t i = 0; i < names.size(); i++) {
+            ts[d][i].d = arena[d] + offs[i];
+            ms[d]->tensors[*names[i]] = std::move(ts[d][i]);
+        }
     return ACM_OK;
+}
+
+// Read-only private mapping of a file, as the reference's readModel
+// (app/model_unix.go:15-34).
+struct FileMap {
+    void *p = MAP_FAILED;
+    size_t len = 0;
+    std::string err;
+    explicit FileMap(const char *path) {
+        const int fd = open(path, O_RDONLY);
+        if (fd < 0) {
+            err = fmt("open %s: %s", path, strerror(errno));
+            return;
+        }
+        struct stat sb;
+        if (fstat(fd, &sb) != 0 || sb.st_size <= 0) {
+            close(fd);
+            err = fmt("stat %s failed", path);
+            return;
+        }
+        len = (size_t)sb.st_size;
+        p = mmap(nullptr, len, PROT_READ, MAP_PRIVATE, fd, 0);
+        close(fd);
+        if (p == MAP_FAILED) {
+            err = fmt("mmap %s failed", path);
+            return;
+        }
+        madvise(p, len, MADV_WILLNEED);
+    }
+    ~FileMap() {
+        if (p != MAP_FAILED) munmap(p, len);
+    }
+    bool ok() const { return p != MAP_FAILED; }
+    const uint8_t *data() const { return static_cast<const uint8_t *>(p); }
+};
+
+// gguf.Parse + infer.Load's metadata and tensor rules + the upload, from the
+// file's bytes, to one model per engine (outs[i] on es[i]).  On failure no
+// model is left and es[0] (or the engine whose model failed) holds the error.
+int load_gguf_bytes(acm_engine *const *es, int n, const uint8_t *data, size_t len, int32_t max_ctx, int32_t max_seqs,
+                    acm_model **outs) {
+    for (int i = 0; i < n; i++) outs[i] = nullptr;
+    gguf::File f;
+    std::string err;
+    int rc = gguf::parse(data, len, f, err);
+    acm_config c;
+    if (!rc) rc = gguf::load_config(f, max_ctx, c, err);
+    if (rc) return set_eerr(es[0], rc, err);
+    std::vector<acm_model *> ms(n, nullptr);
+    for (int i = 0; i < n && !rc; i++) {
+        rc = acm_model_create(es[i], &c, max_seqs, &ms[i]);
+        if (rc && i) es[0]->err = es[i]->err;
+    }
+    std::vector<const std::string *> names;
+    for (const std::string &name : f.order)
+        if (name == "token_embd.weight" || name == "output.weight" || name == "output_norm.weight" ||
+            name.rfind("blk.", 0) == 0)
+            names.push_back(&name);
+    if (!rc) rc = upload_gguf(ms.data(), n, f, names);
+    for (int i = 0; i < n && !rc; i++) {
+        cudaSetDevice(es[i]->device);
+        rc = acm_model_finalize(ms[i]);
+    }
+    if (rc) {
+        for (int i = 0; i < n; i++)
+            if (ms[i]) {
+                if (!ms[i]->err.empty()) es[0]->err = ms[i]->err;
+                acm_model_destroy(ms[i]);
+            }
+        return rc;
+    }
+    for (int i = 0; i < n; i++) outs[i] = ms[i];
+    return ACM_OK;
+}
+
+int config_bytes(const uint8_t *data, size_t len, int32_t max_ctx, acm_config *out, char *err, int32_t errlen) {
+    gguf::File f;
+    std::string e;
+    int rc = gguf::parse(data, len, f, e);
+    if (!rc) rc = gguf::load_config(f, max_ctx, *out, e);
+    if (rc && err && errlen > 0) snprintf(err, (size_t)errlen, "%s", e.c_str());
+    return rc;
 }
 }  // namespace
 
@@ -1251,75 +1390,49 @@ ACM_API int acm_model_load_gguf(acm_engine *e, const char *path, int32_t max_ctx
                                 acm_model **out) {
     if (!e || !path || !out) return ACM_ERR_INVALID;
     *out = nullptr;
-    const int fd = open(path, O_RDONLY);
-    if (fd < 0) return set_eerr(e, ACM_ERR_IO, fmt("open %s: %s", path, strerror(errno)));
-    struct stat sb;
-    if (fstat(fd, &sb) != 0 || sb.st_size <= 0) {
-        close(fd);
-        return set_eerr(e, ACM_ERR_IO, fmt("stat %s failed", path));
-    }
-    const size_t len = (size_t)sb.st_size;
-    // read-only private mapping as the reference's readModel (app/model_unix.go:15-34)
-    void *map = mmap(nullptr, len, PROT_READ, MAP_PRIVATE, fd, 0);
-    close(fd);
-    if (map == MAP_FAILED) return set_eerr(e, ACM_ERR_IO, fmt("mmap %s failed", path));
-    madvise(map, len, MADV_WILLNEED);
-    gguf::File f;
-    std::string err;
-    int rc = gguf::parse(static_cast<const uint8_t *>(map), len, f, err);
-    acm_config c;
-    if (!rc) rc = gguf::load_config(f, max_ctx, c, err);
-    if (rc) {
-        munmap(map, len);
-        return set_eerr(e, rc, err);
-    }
-    acm_model *m = nullptr;
-    rc = acm_model_create(e, &c, max_seqs, &m);
-    if (rc) {
-        munmap(map, len);
-        return rc;
-    }
-    std::vector<const std::string *> names;
-    for (const std::string &name : f.order)
-        if (name == "token_embd.weight" || name == "output.weight" || name == "output_norm.weight" ||
-            name.rfind("blk.", 0) == 0)
-            names.push_back(&name);
-    cudaSetDevice(e->device);
-    rc = upload_gguf(m, f, names);
-    munmap(map, len);
-    if (!rc) rc = acm_model_finalize(m);
-    if (rc) {
-        e->err = m->err;
-        acm_model_destroy(m);
-        return rc;
-    }
-    *out = m;
-    return ACM_OK;
+    FileMap map(path);
+    if (!map.ok()) return set_eerr(e, ACM_ERR_IO, map.err);
+    return load_gguf_bytes(&e, 1, map.data(), map.len, max_ctx, max_seqs, out);
+}
+
+ACM_API int acm_model_load_gguf_mem(acm_engine *e, const void *data, size_t nbytes, int32_t max_ctx, int32_t max_seqs,
+                                    acm_model **out) {
+    if (!e || !data || !out) return ACM_ERR_INVALID;
+    *out = nullptr;
+    return load_gguf_bytes(&e, 1, static_cast<const uint8_t *>(data), nbytes, max_ctx, max_seqs, out);
+}
+
+ACM_API int acm_model_load_gguf_multi(acm_engine *const *es, int32_t n, const char *path, int32_t max_ctx,
+                                      int32_t max_seqs, acm_model **outs) {
+    if (!es || n < 1 || n > 64 || !path || !outs) return ACM_ERR_INVALID;
+    for (int i = 0; i < n; i++)
+        if (!es[i]) return ACM_ERR_INVALID;
+    for (int i = 0; i < n; i++) outs[i] = nullptr;
+    FileMap map(path);
+    if (!map.ok()) return set_eerr(es[0], ACM_ERR_IO, map.err);
+    return load_gguf_bytes(es, n, map.data(), map.len, max_ctx, max_seqs, outs);
 }
 
 ACM_API int acm_load_config(const char *path, int32_t max_ctx, acm_config *out, char *err, int32_t errlen) {
-    auto fail = [&](int rc, const std::string &msg) {
-        if (err && errlen > 0) snprintf(err, (size_t)errlen, "%s", msg.c_str());
-        return rc;
-    };
-    if (!path || !out) return fail(ACM_ERR_INVALID, "null argument");
-    const int fd = open(path, O_RDONLY);
-    if (fd < 0) return fail(ACM_ERR_IO, fmt("open %s: %s", path, strerror(errno)));
-    struct stat sb;
-    if (fstat(fd, &sb) != 0 || sb.st_size <= 0) {
-        close(fd);
-        return fail(ACM_ERR_IO, fmt("stat %s failed", path));
+    if (!path || !out) {
+        if (err && errlen > 0) snprintf(err, (size_t)errlen, "null argument");
+        return ACM_ERR_INVALID;
     }
-    const size_t len = (size_t)sb.st_size;
-    void *map = mmap(nullptr, len, PROT_READ, MAP_PRIVATE, fd, 0);
-    close(fd);
-    if (map == MAP_FAILED) return fail(ACM_ERR_IO, fmt("mmap %s failed", path));
-    gguf::File f;
-    std::string e;
-    int rc = gguf::parse(static_cast<const uint8_t *>(map), len, f, e);
-    if (!rc) rc = gguf::load_config(f, max_ctx, *out, e);
-    munmap(map, len);
-    return rc ? fail(rc, e) : ACM_OK;
+    FileMap map(path);
+    if (!map.ok()) {
+        if (err && errlen > 0) snprintf(err, (size_t)errlen, "%s", map.err.c_str());
+        return ACM_ERR_IO;
+    }
+    return config_bytes(map.data(), map.len, max_ctx, out, err, errlen);
+}
+
+ACM_API int acm_load_config_mem(const void *data, size_t nbytes, int32_t max_ctx, acm_config *out, char *err,
+                                int32_t errlen) {
+    if (!data || !out) {
+        if (err && errlen > 0) snprintf(err, (size_t)errlen, "null argument");
+        return ACM_ERR_INVALID;
+    }
+    return config_bytes(static_cast<const uint8_t *>(data), nbytes, max_ctx, out, err, errlen);
 }
 
 ACM_API int acm_seq_open(acm_model *m, int32_t *seq_out) {
@@ -1789,9 +1902,19 @@ ACM_API int acm_model_bench_gemm(acm_model *m, int32_t ntok, int32_t reps, doubl
     const acm_config &c = m->c;
     cudaStream_t st = m->e->stream;
     const int E = c.n_embd, hd = c.head_dim, qd = c.n_head * hd, kvd = c.n_head_kv * hd, F = c.n_ff;
-    for (const Layer &L : m->layers)
-        if (!use_mma(m, {L.q, L.k, L.v, L.o, L.gate, L.up, L.down}) || F % 64)
+    // the GEMM kind forward_pass takes for each group of weights
+    struct Kinds {
+        bool qkv, o, gu, down;
+    };
+    std::vector<Kinds> kinds;
+    for (const Layer &L : m->layers) {
+        Kinds k{use_mma_dq(m, {L.q, L.k, L.v}, E), use_mma_dq(m, {L.o}, qd),
+                L.gate->type == L.up->type && use_mma_dq(m, {L.gate, L.up}, E), use_mma_dq(m, {L.down}, F)};
+        if ((!k.qkv && !use_mma(m, {L.q, L.k, L.v})) || (!k.o && !use_mma(m, {L.o})) ||
+            (!k.gu && !use_mma(m, {L.gate, L.up})) || (!k.down && !use_mma(m, {L.down})) || F % 64)
             return set_err(m, ACM_ERR_INVALID, "tensor-core GEMM unavailable for this model");
+        kinds.push_back(k);
+    }
     // activation maps: the split buffers as they are (contents do not matter for timing)
     const TensorMap *xe_h = &m->xmap_hi[0], *xe_l = &m->xmap_lo[0];
     const TensorMap *xq_h = &m->xmap_hi[1], *xq_l = &m->xmap_lo[1];
@@ -1801,17 +1924,25 @@ ACM_API int acm_model_bench_gemm(acm_model *m, int32_t ntok, int32_t reps, doubl
     auto pass = [&]() -> int {
         flops = 0;
         nl = 0;
-        for (const Layer &L : m->layers) {
-            MmaGemmSeg sg[3] = {{&L.q->mhi, &L.q->mlo, nullptr, nullptr, qd, EPI_STORE, m->q, qd, L.q_b, nullptr},
-                                {&L.k->mhi, &L.k->mlo, nullptr, nullptr, kvd, EPI_STORE, m->k, kvd, L.k_b, nullptr},
-                                {&L.v->mhi, &L.v->mlo, nullptr, nullptr, kvd, EPI_STORE, m->v, kvd, L.v_b, nullptr}};
-            CK_M(mma_gemm_launch(sg, 3, xe_h, xe_l, ntok, E, st));
-            MmaGemmSeg so{&L.o->mhi, &L.o->mlo, nullptr, nullptr, E, EPI_STORE, m->h, E, nullptr, nullptr};
-            CK_M(mma_gemm_launch(&so, 1, xq_h, xq_l, ntok, qd, st, m->mma_ws, m->mma_ws_floats));
-            MmaGemmSeg sf{&L.gate->mhi, &L.gate->mlo, &L.up->mhi, &L.up->mlo, F, EPI_SWIGLU, m->hb2, F, nullptr, nullptr};
-            CK_M(mma_gemm_launch(&sf, 1, xe_h, xe_l, ntok, E, st));
-            MmaGemmSeg sd{&L.down->mhi, &L.down->mlo, nullptr, nullptr, E, EPI_STORE, m->h, E, nullptr, nullptr};
-            CK_M(mma_gemm_launch(&sd, 1, xf_h, xf_l, ntok, F, st, m->mma_ws, m->mma_ws_floats));
+        for (size_t li = 0; li < m->layers.size(); li++) {
+            const Layer &L = m->layers[li];
+            const Kinds &kd = kinds[li];
+            MmaGemmSeg sg[3] = {{&L.q->mhi, &L.q->mlo, nullptr, nullptr, qd, EPI_STORE, m->q, qd, L.q_b, nullptr,
+                                 L.q->d, nullptr, kd.qkv ? (int)L.q->type : -1},
+                                {&L.k->mhi, &L.k->mlo, nullptr, nullptr, kvd, EPI_STORE, m->k, kvd, L.k_b, nullptr,
+                                 L.k->d, nullptr, kd.qkv ? (int)L.k->type : -1},
+                                {&L.v->mhi, &L.v->mlo, nullptr, nullptr, kvd, EPI_STORE, m->v, kvd, L.v_b, nullptr,
+                                 L.v->d, nullptr, kd.qkv ? (int)L.v->type : -1}};
+            CK_M(mma_run(sg, 3, xe_h, xe_l, ntok, E, st));
+            MmaGemmSeg so{&L.o->mhi, &L.o->mlo, nullptr, nullptr, E, EPI_STORE, m->h, E, nullptr, nullptr,
+                          L.o->d, nullptr, kd.o ? (int)L.o->type : -1};
+            CK_M(mma_run(&so, 1, xq_h, xq_l, ntok, qd, st, m->mma_ws, m->mma_ws_floats));
+            MmaGemmSeg sf{&L.gate->mhi, &L.gate->mlo, &L.up->mhi, &L.up->mlo, F, EPI_SWIGLU, m->hb2, F, nullptr, nullptr,
+                          L.gate->d, L.up->d, kd.gu ? (int)L.gate->type : -1};
+            CK_M(mma_run(&sf, 1, xe_h, xe_l, ntok, E, st));
+            MmaGemmSeg sd{&L.down->mhi, &L.down->mlo, nullptr, nullptr, E, EPI_STORE, m->h, E, nullptr, nullptr,
+                          L.down->d, nullptr, kd.down ? (int)L.down->type : -1};
+            CK_M(mma_run(&sd, 1, xf_h, xf_l, ntok, F, st, m->mma_ws, m->mma_ws_floats));
             flops += 2.0 * ntok * ((double)(qd + 2 * kvd) * E + (double)E * qd + 2.0 * F * E + (double)E * F);
             nl += 4;
         }
@@ -1989,6 +2120,21 @@ ACM_API int acm_matmul_dev(acm_engine *e, uint32_t ggml_type, const void *d_w, i
     if (gemv_supported((int)ggml_type, k, m)) {
         GemvSegDesc sg{d_w, nullptr, (int)ggml_type, n, EPI_STORE, d_y, (int)n, nullptr, nullptr};
         CK_E(gemv_launch(&sg, 1, d_x, (int)k, k, m, nullptr, 0.f, e->num_sms, e->stream));
+    } else if (k % 256 == 0 && dq_type((int)ggml_type) && mma_available()) {
+        // tensor-core path, W dequantized in the kernel: split x only
+        const size_t xbs = al256((size_t)rows64(m) * k * 2);
+        const size_t wsf = std::min<size_t>(4 * (size_t)m * n, (size_t)148 * 128 * 64);
+        uint8_t *s2 = nullptr;
+        if (int rc = scratch2(e, 2 * xbs + wsf * 4, &s2)) return rc;
+        uint8_t *xhi = s2, *xlo = s2 + xbs;
+        float *ws = reinterpret_cast<float *>(xlo + xbs);
+        CK_E(split_act_launch(d_x, (int)k, m, (int)k, xhi, xlo, e->stream));
+        TensorMap mxh, mxl;
+        if (!bf16_map(&mxh, xhi, m, k) || !bf16_map(&mxl, xlo, m, k))
+            return set_eerr(e, ACM_ERR_CUDA, "tensor map encoding failed");
+        MmaGemmSeg sg{nullptr, nullptr, nullptr, nullptr, n, EPI_STORE, d_y, (int)n, nullptr, nullptr,
+                      d_w, nullptr, (int)ggml_type};
+        CK_E(mma_dq_launch(&sg, 1, &mxh, &mxl, m, (int)k, e->stream, ws, wsf));
     } else if (k % 64 == 0 && mma_available()) {
         // tensor-core path: split W and x to bf16 hi/lo in the second scratch
         const size_t wbs = al256((size_t)rows64(n) * k * 2), xbs = al256((size_t)rows64(m) * k * 2);

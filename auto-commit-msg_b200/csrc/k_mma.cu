@@ -41,6 +41,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "launch.cuh"
+#include "mma_dev.cuh"
 #include "quant.cuh"
 
 namespace acm {
@@ -58,55 +59,14 @@ constexpr int MMA_THREADS = 192;
 constexpr int MMA_SMEM = MST * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr uint32_t TMEM_COLS = 64;
 
-// ---- PTX wrappers ----
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                       uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-__device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
-}
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, rows of 128
-// bytes in 8-row (1024-byte) atoms -- the layout TMA writes with
-// CU_TENSOR_MAP_SWIZZLE_128B and a 64-element bf16 box row.  Fields: start
-// address >> 4 [0,14), leading byte offset (1: unused for swizzled K-major)
-// [16,30), stride byte offset 1024 >> 4 [32,46), version 1 [46,48), layout
-// 2 = SWIZZLE_128B [61,64).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-// Instruction descriptor, kind::f16: fp32 accumulator [4,6)=1, A and B bf16
-// [7,10)=1 [10,13)=1, both K-major, N >> 3 at [17,23), M >> 4 at [24,29).
-constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MBN >> 3) << 17) |
-                           ((uint32_t)(MBM >> 4) << 24);
+constexpr uint32_t IDESC = mma::idesc_bf16(MBM, MBN);
+using mma::tma_load_2d;
+using mma::tc_fence_before;
+using mma::tc_fence_after;
+using mma::tc_commit;
+using mma::tc_mma;
+using mma::tc_ld16;
+using mma::sw128_desc;
 
 }  // namespace
 
@@ -247,7 +207,9 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_mma_gemm(const __grid_consta
     } else if (warp >= 2) {
         // ---- epilogue ----
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
-        const bool ok = mbar_wait(accf, 0);
+        // the four epilogue warps decide together: the pair exchange below
+        // meets at named barriers
+        const bool ok = named_and(1, 128, mbar_wait(accf, 0));
         tc_fence_after();
         if (ok) {
             const int lrow = q * 32 + lane;  // accumulator row (TMEM lane)
@@ -664,14 +626,19 @@ cudaError_t mma_gemm_batched_launch(const MmaGemmSeg *segs, int nseg, const Tens
     cudaError_t e = launch_pdl(k_mma_gemm, dim3(tiles, bt.n, a.ksplit), dim3(MMA_THREADS), MMA_SMEM, st, a);
     if (e != cudaSuccess) return e;
     if (a.ksplit > 1) {
-        const int64_t total = (int64_t)m * segs[0].n;
-        const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
-        e = launch_pdl(k_split_reduce, dim3(grid), dim3(256), 0, st, (const float *)ws, a.ksplit, m, (int)segs[0].n,
-                       segs[0].y, segs[0].ldy, segs[0].epi, segs[0].bias, segs[0].yrow);
+        e = split_reduce_launch(ws, a.ksplit, m, (int)segs[0].n, segs[0].y, segs[0].ldy, segs[0].epi, segs[0].bias,
+                                segs[0].yrow, st);
         if (e != cudaSuccess) return e;
         return launched(2);
     }
     return launched(1);
+}
+
+cudaError_t split_reduce_launch(const float *ws, int ks, int m, int n, float *y, int ldy, int epi, const float *bias,
+                                const int32_t *yrow, cudaStream_t st) {
+    const int64_t total = (int64_t)m * n;
+    const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
+    return launch_pdl(k_split_reduce, dim3(grid), dim3(256), 0, st, ws, ks, m, n, y, ldy, epi, bias, yrow);
 }
 
 }  // namespace acm

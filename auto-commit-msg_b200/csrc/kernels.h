@@ -124,6 +124,9 @@ struct MmaGemmSeg {
     int ldy;
     const float *bias;
     const int32_t *yrow;
+    // the weights as GGUF rows, for mma_dq_launch (dequantized in the kernel)
+    const void *w = nullptr, *w2 = nullptr;
+    int wtype = -1;
 };
 // ws (optional, ws_floats floats): workspace for split-K partial sums, used
 // when the output tiles would leave most SMs idle.
@@ -142,6 +145,16 @@ struct MmaBatch {
 cudaError_t mma_gemm_batched_launch(const MmaGemmSeg *segs, int nseg, const TensorMap *x_hi, const TensorMap *x_lo,
                                     int m, int k, const MmaBatch &bt, cudaStream_t st, float *ws = nullptr,
                                     size_t ws_floats = 0);
+
+// Tensor-core GEMM with the weights dequantized in shared memory (k_mma_dq.cu):
+// the segments' w / w2 / wtype (one quantized type, or Q4_K with Q6_K), K a
+// multiple of 256; otherwise as mma_gemm_launch.
+bool dq_type(int t);
+cudaError_t mma_dq_launch(const MmaGemmSeg *segs, int nseg, const TensorMap *x_hi, const TensorMap *x_lo, int m, int k,
+                          cudaStream_t st, float *ws = nullptr, size_t ws_floats = 0);
+// Split-K epilogue: y[tok][n] (epi)= bias[n] + the ks partial sums of ws, in order.
+cudaError_t split_reduce_launch(const float *ws, int ks, int m, int n, float *y, int ldy, int epi, const float *bias,
+                                const int32_t *yrow, cudaStream_t st);
 
 // Prefill attention on the tensor cores: operand preparation (k_attn_split)
 // and the softmax between S = Q.K^T and O = P.V (k_attn_softmax).

@@ -11,7 +11,7 @@ from __future__ import annotations
 
 import ctypes as C
 from dataclasses import dataclass
-from typing import Callable, Optional, Sequence
+from typing import Callable, List, Optional, Sequence
 
 import numpy as np
 
@@ -278,6 +278,51 @@ def Load(path: str, maxCtx: int = 0, engine: Optional[Engine] = None, max_seqs: 
             e.close()
         raise AcmError(rc, msg)
     return Model(e, h, own)
+
+
+def LoadBytes(data, maxCtx: int = 0, engine: Optional[Engine] = None, max_seqs: int = 1,
+              device: int = 0) -> Model:
+    """infer.Load(gguf.Parse(data), maxCtx) (model.go:90-203, gguf.go:121-174)
+    over a GGUF image in host memory (bytes, a bytearray, an mmap or a numpy
+    uint8 array): what the reference's host holds after readModel or for its
+    embedded model (app/app.go:77-89)."""
+    buf = np.frombuffer(data, dtype=np.uint8)
+    own = engine is None
+    e = engine or Engine(device)
+    h = C.c_void_p()
+    rc = _lib.lib().acm_model_load_gguf_mem(e.handle, buf.ctypes.data_as(C.c_void_p), buf.nbytes, maxCtx,
+                                            max_seqs, C.byref(h))
+    if rc:
+        msg = _lib.lib().acm_engine_error(e.handle).decode()
+        if own:
+            e.close()
+        raise AcmError(rc, msg)
+    return Model(e, h, own)
+
+
+def LoadMulti(path: str, engines: Sequence[Engine], maxCtx: int = 0, max_seqs: int = 1) -> List[Model]:
+    """One model per engine from one mapping of the file: parsed once, each
+    staging chunk read from the mapping once and copied to every engine's
+    device (no reference counterpart; app/model_unix.go:15-34 maps it once per
+    process).  The engines stay the caller's."""
+    n = len(engines)
+    es = (C.c_void_p * n)(*[e.handle for e in engines])
+    hs = (C.c_void_p * n)()
+    rc = _lib.lib().acm_model_load_gguf_multi(es, n, path.encode(), maxCtx, max_seqs, hs)
+    if rc:
+        raise AcmError(rc, _lib.lib().acm_engine_error(engines[0].handle).decode())
+    return [Model(engines[i], C.c_void_p(hs[i]), False) for i in range(n)]
+
+
+def LoadConfigBytes(data, maxCtx: int = 0) -> Config:
+    """LoadConfig over a GGUF image in host memory."""
+    buf = np.frombuffer(data, dtype=np.uint8)
+    cfg = Config()
+    err = C.create_string_buffer(512)
+    rc = _lib.lib().acm_load_config_mem(buf.ctypes.data_as(C.c_void_p), buf.nbytes, maxCtx, C.byref(cfg), err, 512)
+    if rc:
+        raise AcmError(rc, err.value.decode())
+    return cfg
 
 
 def LoadConfig(path: str, maxCtx: int = 0) -> Config:

@@ -140,10 +140,30 @@ ACM_API int acm_model_config(acm_model *m, acm_config *out);
 ACM_API int acm_model_load_gguf(acm_engine *e, const char *path, int32_t max_ctx, int32_t max_seqs,
                                 acm_model **out);
 
+/* acm_model_load_gguf over a GGUF image already in host memory (an mmap, or
+ * bytes embedded in the binary as the reference's fat build does,
+ * app/app.go:77-89): the same parse, rules and upload; `data` is not retained.
+ * Replaces infer.Load(gguf.Parse(data), maxCtx) (model.go:90-203) for a host
+ * that holds the file's bytes. */
+ACM_API int acm_model_load_gguf_mem(acm_engine *e, const void *data, size_t nbytes, int32_t max_ctx,
+                                    int32_t max_seqs, acm_model **out);
+
+/* One model per engine from one mapping of the file (no reference
+ * counterpart; the reference maps the file once per process,
+ * app/model_unix.go:15-34): parsed once, every staging chunk filled once on
+ * the host and copied to each engine's device (engines may share a device).
+ * outs[i] is created on es[i]; on failure none is left and es[0] holds the
+ * error.  1 <= n <= 64. */
+ACM_API int acm_model_load_gguf_multi(acm_engine *const *es, int32_t n, const char *path, int32_t max_ctx,
+                                      int32_t max_seqs, acm_model **outs);
+
 /* Parse a GGUF file and derive its configuration without touching a device:
  * gguf.Parse (gguf.go:121-174) plus the metadata rules of infer.Load
  * (model.go:91-151).  err receives a message on failure. */
 ACM_API int acm_load_config(const char *path, int32_t max_ctx, acm_config *out, char *err, int32_t errlen);
+/* acm_load_config over a GGUF image in host memory. */
+ACM_API int acm_load_config_mem(const void *data, size_t nbytes, int32_t max_ctx, acm_config *out, char *err,
+                                int32_t errlen);
 
 /* Sequence slots.  A slot is one infer.Model's sequence state (pos + KV). */
 ACM_API int acm_seq_open(acm_model *m, int32_t *seq_out);

@@ -45,6 +45,19 @@ def test_config_matches_oracle(acm, oracle, tiny_models, name, ctx):
         assert getattr(c, f) == getattr(o, f), f
 
 
+@pytest.mark.parametrize("name", ["qwen3", "llama_q5"])
+def test_config_from_bytes(acm, tiny_models, name):
+    """acm_load_config_mem over the file's bytes equals the path entry."""
+    with open(tiny_models[name], "rb") as f:
+        data = f.read()
+    for ctx in (0, 100):
+        a, b = acm.LoadConfig(tiny_models[name], ctx), acm.LoadConfigBytes(data, ctx)
+        for f in CFG_FIELDS:
+            assert getattr(a, f) == getattr(b, f), f
+    with pytest.raises(acm.AcmError, match="truncated"):
+        acm.LoadConfigBytes(data[:40])
+
+
 def test_config_rules(acm, synth, tmp_path):
     # llama with freq_base >= 5e5 and no scaling keys gets llama3 defaults (model.go:126-134)
     s = synth.ModelShape("llama", 1, 256, 4, 2, 64, 256, 300, ctx=512, rope_base=5e5)
@@ -81,6 +94,9 @@ def test_parse_errors(acm, tmp_path):
         p.write_bytes(blob)
         with pytest.raises(acm.AcmError) as ei:
             acm.LoadConfig(str(p))
+        assert msg in str(ei.value) and ei.value.code == code
+        with pytest.raises(acm.AcmError) as ei:
+            acm.LoadConfigBytes(blob)
         assert msg in str(ei.value) and ei.value.code == code
 
 

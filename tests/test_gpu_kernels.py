@@ -87,6 +87,15 @@ def test_gemm_prefill_shapes(eng, oracle, synth, typ, shape):
     _check_matmul(eng, oracle, synth, typ, n, k, 389, seed=k + n + typ, tol=MMA_TOL)
 
 
+@pytest.mark.parametrize("typ", [8, 12, 14])
+@pytest.mark.parametrize("m", [150, 389])
+def test_gemm_wide_token_tiles(eng, oracle, synth, typ, m):
+    """8192 rows: 64 row tiles, so the in-kernel dequant GEMM widens its token
+    tiles to 2 or 3 blocks of 64 tokens (uneven: 1+2 blocks at 150 tokens,
+    3+2+2 at 389; Q8_0's wider rows limit it to 2 blocks)."""
+    _check_matmul(eng, oracle, synth, typ, 8192, 512, m, seed=typ + m, tol=MMA_TOL)
+
+
 @pytest.mark.parametrize("typ", [0, 1, 2, 6, 8])
 def test_gemm_k_not_64(eng, oracle, synth, typ):
     """K = 1056 (a multiple of 32, not of 64): the CUDA-core GEMM."""
