@@ -9,9 +9,13 @@
 // accumulation (the lo.lo term is below 2^-16 of the product): three MMAs per
 // K step, relative error ~1e-5.
 //
-// Layout.  Dequantization (exact, tensor.go:55-226) happens once per weight
-// tensor into two bf16 arrays (the "split cache", 4 bytes per weight, built
-// on first use and kept in HBM); activations are split per call.  Both are
+// Layout.  This kernel reads weights that are already bf16 pairs: F16/F32
+// weights and quantized ones whose K is not a multiple of 256 are dequantized
+// (exact, tensor.go:55-226) once per tensor into two bf16 arrays (the "split
+// cache", 4 bytes per weight, built on first use and kept in HBM); quantized
+// weights with K % 256 == 0 take k_mma_dq.cu, which dequantizes in shared
+// memory and keeps no cache.  The attention GEMMs (S = Q.K^T, O = P.V) run
+// here on split operands prepared per call, as do the activations.  Both are
 // stored 64x64-blocked -- element (r, c) at ((r/64)*(K/64) + c/64)*4096 +
 // (r%64)*64 + c%64 -- so each TMA box is one contiguous 8 KB read (a
 // row-major [n][K] box gathers 64 pieces of 128 bytes from 64 DRAM pages),

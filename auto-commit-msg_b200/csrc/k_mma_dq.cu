@@ -19,7 +19,9 @@
 //   warp 1       allocates 128 TMEM columns; lane 0 issues the three
 //                tcgen05.mma (hi.hi, hi.lo, lo.hi; M=128, N=128, K=16) per 16
 //                K-elements and frees stages with tcgen05.commit;
-//   warps 2..5   epilogue (their TMEM lane quadrants), as k_mma.cu.
+//   warps 2..17  then the epilogue: each reads its TMEM lane quadrant
+//                (warp % 4) for a quarter of the token columns; a SwiGLU
+//                pair's gate and up rows meet in shared memory.
 // A tile is 128 weight rows x 128 tokens, so each dequantized weight feeds
 // 128 tokens' products: per 64 K-elements the CTA reads the rows' quantized
 // bytes (4.6 KB for Q4_K) and 32 KB of activation splits, against 48 KB of
@@ -306,7 +308,7 @@ __global__ void __launch_bounds__(DQ_THREADS, 1) k_mma_dq(const __grid_constant_
             tc_commit(accf);
         }
     } else {
-        // ---- dequantizers (warps 2..17), then the epilogue (warps 2..5) ----
+        // ---- dequantizers (warps 2..17), then the epilogue ----
         const int q = (warp - 2) * 32 + lane;  // 0..511: row q / 4, run half, 16-element sub
         const int row = q >> 2, half = (q >> 1) & 1, sub = q & 1;
         const int lr = S.pair ? (row & 63) : row;
@@ -365,59 +367,61 @@ __global__ void __launch_bounds__(DQ_THREADS, 1) k_mma_dq(const __grid_constant_
             if (lane == 0) mbar_arrive(&afull[as]);
         }
         cp_async_wait_all();  // no copy lands after the CTA exits
-        if (warp < 6) {
-            // ---- epilogue ----
-            const int qd = warp & 3;  // TMEM lane quadrant this warp may access
-            const bool fin = named_and(1, 128, mbar_wait(accf, 0));
-            tc_fence_after();
-            if (fin) {
-                const int lrow = qd * 32 + lane;
-                // pair exchange [64][ntile + 1] floats in the idle B stages
-                // (64 * (64 * bmax + 1) * 4 <= DBST * 2 * bhalf bytes)
-                float *xch = reinterpret_cast<float *>(bstg);
-                for (int c0 = 0; c0 < ntile; c0 += 16) {
+        // ---- epilogue, on all dequantizer warps: a warp reads its TMEM lane
+        // quadrant (warp % 4) and the column chunks cg*16 + 64 i ----
+        const int qd = warp & 3, cg = (warp - 2) >> 2;
+        const int et = tid - 64;  // 0 .. DQ_WARPS * 32 - 1
+        const bool fin = named_and(1, DQ_WARPS * 32, mbar_wait(accf, 0));
+        tc_fence_after();
+        if (fin) {
+            const int lrow = qd * 32 + lane;  // accumulator row (TMEM lane)
+            const uint32_t tl = tmem + ((uint32_t)(qd * 32) << 16);
+            if (S.pair) {
+                // gate rows (lanes 0..63) and up rows (64..127) to the idle A/B
+                // stages, [64][ntile + 1] floats each (2 * 64 * 193 * 4 bytes
+                // <= the 64 KB of A stages + 2 * DBST * DBOX), then every
+                // thread takes outputs with consecutive rows (coalesced stores)
+                float *xg = reinterpret_cast<float *>(astg), *xu = xg + 64 * (ntile + 1);
+                float *xr = (qd < 2 ? xg + lrow * (ntile + 1) : xu + (lrow - 64) * (ntile + 1));
+                for (int c0 = cg * 16; c0 < ntile; c0 += 64) {
                     float v[16];
-                    tc_ld16(tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)c0, v);
-                    if (S.pair) {
-                        if (qd >= 2)
+                    tc_ld16(tl + (uint32_t)c0, v);
 #pragma unroll
-                            for (int j = 0; j < 16; j++) xch[(lrow - 64) * (ntile + 1) + c0 + j] = v[j];
-                        named_sync(1, 128);
-                        if (qd < 2) {
-                            const int n = row0 + lrow;
-#pragma unroll
-                            for (int j = 0; j < 16; j++) {
-                                const int tok = tok0 + c0 + j;
-                                if (n < S.n && tok < A.m) {
-                                    const float g = v[j], u = xch[lrow * (ntile + 1) + c0 + j];
-                                    const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, fast_exp(-g)));
-                                    float *yp = S.y + (int64_t)(S.yrow ? S.yrow[tok] : tok) * S.ldy + n;
-                                    *yp = __fmul_rn(__fmul_rn(g, sg), u);
-                                }
-                            }
-                        }
-                        named_sync(1, 128);
+                    for (int j = 0; j < 16; j++) xr[c0 + j] = v[j];
+                }
+                named_sync(1, DQ_WARPS * 32);
+                for (int i = et; i < 64 * ntile; i += DQ_WARPS * 32) {
+                    const int r = i & 63, c = i >> 6;
+                    const int n = row0 + r, tok = tok0 + c;
+                    if (n < S.n && tok < A.m) {
+                        const float g = xg[r * (ntile + 1) + c], u = xu[r * (ntile + 1) + c];
+                        const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, fast_exp(-g)));
+                        float *yp = S.y + (int64_t)(S.yrow ? S.yrow[tok] : tok) * S.ldy + n;
+                        *yp = __fmul_rn(__fmul_rn(g, sg), u);
+                    }
+                }
+            } else {
+                const int n = row0 + lrow;
+                for (int c0 = cg * 16; c0 < ntile; c0 += 64) {
+                    float v[16];
+                    tc_ld16(tl + (uint32_t)c0, v);  // warp-wide: before any lane-dependent branch
+                    if (n >= S.n) {
                     } else if (A.ksplit > 1) {
-                        const int n = row0 + lrow;
-                        if (n < S.n)
 #pragma unroll
-                            for (int j = 0; j < 16; j++) {
-                                const int tok = tok0 + c0 + j;
-                                if (tok < A.m) A.ws[((int64_t)blockIdx.z * A.m + tok) * S.n + n] = v[j];
-                            }
+                        for (int j = 0; j < 16; j++) {
+                            const int tok = tok0 + c0 + j;
+                            if (tok < A.m) A.ws[((int64_t)blockIdx.z * A.m + tok) * S.n + n] = v[j];
+                        }
                     } else {
-                        const int n = row0 + lrow;
-                        if (n < S.n) {
-                            const float b = S.bias ? S.bias[n] : 0.f;
+                        const float b = S.bias ? S.bias[n] : 0.f;
 #pragma unroll
-                            for (int j = 0; j < 16; j++) {
-                                const int tok = tok0 + c0 + j;
-                                if (tok < A.m) {
-                                    float *yp = S.y + (int64_t)(S.yrow ? S.yrow[tok] : tok) * S.ldy + n;
-                                    const float val = S.bias ? v[j] + b : v[j];
-                                    if (S.epi == EPI_ADD) *yp = *yp + val;
-                                    else *yp = val;
-                                }
+                        for (int j = 0; j < 16; j++) {
+                            const int tok = tok0 + c0 + j;
+                            if (tok < A.m) {
+                                float *yp = S.y + (int64_t)(S.yrow ? S.yrow[tok] : tok) * S.ldy + n;
+                                const float val = S.bias ? v[j] + b : v[j];
+                                if (S.epi == EPI_ADD) *yp = *yp + val;
+                                else *yp = val;
                             }
                         }
                     }

@@ -120,8 +120,10 @@ ACM_API int acm_engine_set_wait_limit(acm_engine *e, int64_t polls);
 ACM_API int acm_model_create(acm_engine *e, const acm_config *cfg, int32_t max_seqs, acm_model **out);
 
 /* Copy one GGUF tensor's bytes UNCHANGED to HBM (the blocks stay in ggml
- * layout and the decode matvecs read them as they are; the tensor-core GEMM
- * of prefill builds a bf16 hi/lo copy of a linear weight on first use).  dims[0] is the
+ * layout: the decode matvecs read them as they are, and the tensor-core GEMM
+ * of prefill dequantizes them in shared memory; only F16/F32 linear weights,
+ * or quantized ones whose K is not a multiple of 256, get a bf16 hi/lo copy
+ * built on first use).  dims[0] is the
  * innermost dimension as in gguf.Tensor.Dims (gguf.go:42-49).  host_bytes may
  * point into an mmap and is not retained. */
 ACM_API int acm_model_add_tensor(acm_model *m, const char *name, uint32_t ggml_type, const uint64_t *dims,
