@@ -263,10 +263,12 @@ def run_ours(args, rank, world, local):
     sec, nbytes, nl = bench_gemv(acm, m)
     peak, peak_kind = peaks()
     achieved = nbytes / sec / 1e9
-    traffic = None
+    traffic = prefill_traffic = None
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            traffic = json.load(f).get("k_gemv_decode_pass_bytes")
+            tj = json.load(f)
+        traffic = tj.get("k_gemv_decode_pass_bytes")
+        prefill_traffic = tj.get("k_mma_dq_prefill_pass_bytes")
     except Exception:
         pass
     # prefill: the tensor-core GEMM launches of one 389-token prefill
@@ -276,11 +278,13 @@ def run_ours(args, rank, world, local):
         gsec, gfl, gnl = g
         tpk, tpk_kind = tensor_peak()
         pipe = 3 * gfl / gsec / 1e12  # three bf16 products per K step on the tensor pipe
-        prefill_roof = {"bound": "tensor", "kernel": "k_mma_gemm (all GEMM launches of one 389-token prefill)",
+        prefill_roof = {"bound": "tensor", "kernel": "k_mma_dq (all GEMM launches of one 389-token prefill)",
                         "achieved": round(pipe, 1), "peak": tpk, "unit": "TFLOP/s", "frac": round(pipe / tpk, 4),
                         "peak_kind": tpk_kind, "useful_tflops": round(gfl / gsec / 1e12, 1),
                         "note": "achieved counts the 3 bf16 products of the hi/lo split (3 x 2*M*N*K per GEMM)",
-                        "ms_per_pass": round(gsec * 1e3, 3), "launches_per_pass": gnl, "traffic": None}
+                        "ms_per_pass": round(gsec * 1e3, 3), "launches_per_pass": gnl, "traffic": prefill_traffic,
+                        "traffic_source": "profiles/traffic.json (DRAM bytes of one layer's four launches, one ncu "
+                                          "capture with warm caches, x 28 layers)"}
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(1e3 * dev_max / args.steps, 3), "higher_is_better": True,
@@ -293,11 +297,12 @@ def run_ours(args, rank, world, local):
         "e2e": {"value": round(world * args.steps * GEN_TOKENS / wall_max, 2), "unit": "tok/s",
                 "h2d_bytes_per_step": PROMPT_LEN * 4 + 128, "d2h_bytes_per_step": GEN_TOKENS * 4,
                 "note": "acm_generate through the C ABI: host prompt in, host ids out, prefill included"},
-        "roofline": {"bound": "hbm", "kernel": "k_gemv (all GEMV launches of one decode token)",
+        "roofline": {"bound": "hbm", "kernel": "k_gemv1 + k_gemv (all 113 matvec launches of one decode token)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "bytes_per_pass": int(nbytes), "launches_per_pass": nl, "traffic": traffic,
-                     "traffic_source": "profiles/traffic.json (DRAM bytes of the same pass, one ncu capture)"},
+                     "traffic_source": "profiles/traffic.json (DRAM bytes with warm caches: one layer's four k_gemv1 "
+                                       "launches x 28 + the lm_head launch, ncu captures)"},
         "prefill_roofline": prefill_roof,
         "gpu_launches": tot_launches,
         "clocks": ck,
