@@ -408,6 +408,9 @@ int attention_prefill_mma(acm_model *m, int layer, int seq, int pos0, int ntok) 
     bq.a_stride = (Lp / 64) * (hd / 64) * 64;
     bq.b_stride = (int)(rq / 64) * (hd / 64) * 64;
     bq.rbatch = rows;
+    bq.causal = 1;  // key tiles above the diagonal: never read by the softmax
+    bq.cntok = ntok;
+    bq.cpos0 = pos0;
     CK_M(mma_gemm_batched_launch(&sq, 1, &qh, &ql, rows, hd, bq, st));
     CK_M(attn_softmax_launch(o, st));
     // att[t][(g*G + h)*hd + d] = P[g][h*ntok + t] . Vt[g][d]
@@ -420,6 +423,9 @@ int attention_prefill_mma(acm_model *m, int layer, int seq, int pos0, int ntok) 
     bv.rmul = nh;
     bv.rdiv = 1;
     bv.rbatch = G;
+    bv.causal = 2;  // P is zero past each token's position
+    bv.cntok = ntok;
+    bv.cpos0 = pos0;
     CK_M(mma_gemm_batched_launch(&sv, 1, &ph, &pl, rows, Lp, bv, st));
     return ACM_OK;
 }

@@ -98,6 +98,7 @@ struct MmaArgs {
     // rows, and the output row of token `tok` of batch b:
     // (rmod ? (tok % rmod) * rmul + (tok / rmod) * rdiv : tok) + b * rbatch
     int a_bstride, b_bstride, rmod, rmul, rdiv, rbatch;
+    int causal, cntok, cpos0;  // MmaBatch::causal
     // split-K (blockIdx.z = K slice): partial sums to ws[slice][tok][n]
     int ksplit;
     float *ws;
@@ -130,7 +131,15 @@ __global__ void __launch_bounds__(MMA_THREADS, 1) k_mma_gemm(const __grid_consta
     const int batch = blockIdx.y;
     // this CTA's K blocks: all of them, or its slice under split-K
     const int KTA = A.k / MBK;  // K blocks of the operands (their layout)
-    const int kb0 = (int)((int64_t)KTA * blockIdx.z / A.ksplit), kb1 = (int)((int64_t)KTA * (blockIdx.z + 1) / A.ksplit);
+    const int kb0 = (int)((int64_t)KTA * blockIdx.z / A.ksplit);
+    int kb1 = (int)((int64_t)KTA * (blockIdx.z + 1) / A.ksplit);
+    if (A.causal) {
+        // the last key any query row of this token tile attends
+        const int tl = min(tok0 + MBN, A.m) - 1;
+        const int kmax = A.cpos0 + (tok0 / A.cntok != tl / A.cntok ? A.cntok - 1 : tl % A.cntok);
+        if (A.causal == 1 && row0 > kmax) return;  // the whole CTA: every score of the tile is masked
+        if (A.causal == 2) kb1 = max(kb0, min(kb1, kmax / MBK + 1));
+    }
     const int KT = kb1 - kb0;
 
     if (tid == 0) {
@@ -582,6 +591,10 @@ cudaError_t mma_gemm_batched_launch(const MmaGemmSeg *segs, int nseg, const Tens
     a.rmul = bt.rmul;
     a.rdiv = bt.rdiv;
     a.rbatch = bt.rbatch;
+    if (bt.causal && bt.cntok < 1) return cudaErrorInvalidValue;
+    a.causal = bt.causal;
+    a.cntok = bt.cntok;
+    a.cpos0 = bt.cpos0;
     a.nseg = nseg;
     a.m = m;
     a.k = k;

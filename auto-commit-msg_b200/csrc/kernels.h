@@ -141,6 +141,12 @@ struct MmaBatch {
     int n = 1;
     int a_stride = 0, b_stride = 0;
     int rmod = 0, rmul = 0, rdiv = 0, rbatch = 0;
+    // causal attention (token tok is query row tok % cntok at position
+    // cpos0 + tok % cntok, attending keys 0 .. that position): 1 -- the
+    // weight rows are keys (S = Q.K^T), tiles whose keys are all masked are
+    // skipped (their scores are never read); 2 -- K runs over keys (O = P.V),
+    // each tile stops after its last attended key (P is zero beyond it)
+    int causal = 0, cntok = 0, cpos0 = 0;
 };
 cudaError_t mma_gemm_batched_launch(const MmaGemmSeg *segs, int nseg, const TensorMap *x_hi, const TensorMap *x_lo,
                                     int m, int k, const MmaBatch &bt, cudaStream_t st, float *ws = nullptr,
