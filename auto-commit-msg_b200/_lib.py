@@ -94,8 +94,6 @@ SIGNATURES = {
     "acm_model_bench_gemm": (C.c_int, [P, C.c_int32, C.c_int32, C.POINTER(C.c_double), C.POINTER(C.c_double),
                                        C.POINTER(C.c_int32)]),
     "acm_serve": (C.c_int, [P, C.POINTER(CRequest), C.c_int32, C.c_int32, C.c_int32, C.POINTER(CStats)]),
-    "acm_model_trace": (C.c_int, [P, C.c_int32]),
-    "acm_model_trace_read": (C.c_int, [P, P, C.c_int64, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
     "acm_model_debug_layers": (C.c_int, [P, C.c_int32]),
     "acm_model_debug_layers_read": (C.c_int, [P, P, C.c_int64]),
     "acm_model_trace_gemv": (C.c_int, [P, C.c_int32]),

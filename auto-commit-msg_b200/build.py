@@ -22,7 +22,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-rdc=true", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
          "--expt-relaxed-constexpr", "-I", os.path.join(ROOT, "include"), "-I", CSRC]
-SOURCES = ["k_gemv.cu", "k_gemv1.cu", "k_misc.cu", "k_attn.cu", "k_gemm.cu", "k_decode.cu", "k_mma.cu", "k_mma_dq.cu", "k_noalloc.cu", "engine.cu", "gguf_host.cpp"]
+SOURCES = ["k_gemv.cu", "k_gemv1.cu", "k_misc.cu", "k_attn.cu", "k_gemm.cu", "k_mma.cu", "k_mma_dq.cu", "k_noalloc.cu", "engine.cu", "gguf_host.cpp"]
 
 
 def _deps():

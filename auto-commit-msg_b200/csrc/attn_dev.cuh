@@ -1,6 +1,6 @@
-// attn_dev.cuh -- device helpers shared by the attention kernels and the
-// persistent decode kernel: paged cache addressing and the per-head
-// RMSNorm + RoPE of model.go:362-382.
+// attn_dev.cuh -- device helpers of the attention kernels: paged cache
+// addressing, the per-head RMSNorm + RoPE of model.go:362-382 and the
+// batch-1 decode attention item.
 #pragma once
 #include <float.h>
 
@@ -143,8 +143,8 @@ __device__ __forceinline__ void dec_item_offsets(const KVDesc &kv, int seq, int 
 // asynchronous copies (one round trip for every head's rows while hn x
 // slices fits dec_merge_rows, else per head in tiles); per-head maxima and
 // weights are warp reductions, the outputs one (head, dim) per thread.
-// Register use stays small so the item also runs inside the persistent
-// decode kernel's 96-register budget.  KH: the cache holds IEEE half (the
+// Register use stays small (a fast CTA launch, several items per SM).  KH:
+// the cache holds IEEE half (the
 // reduced-precision cache); its rows are loaded into registers first,
 // widened into the same fp32 staging rows once the query heads are ready,
 // and the appended key/value are rounded to half before they are used.

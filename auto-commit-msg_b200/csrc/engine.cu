@@ -167,17 +167,10 @@ struct acm_model {
     unsigned long long *d_amax = nullptr;  // per-token argmax keys (greedy decode)
     int *d_attn_cnt = nullptr;              // decode attention split counters
     int dec_nsplit = 1;                     // chunk capacity of the decode attention
-    // persistent decode kernel (batch 1): per-CTA phase table + grid barrier
-    DecPlan dplan;
-    int dplan_state = 0;                    // 0 untried, 1 usable, -1 unavailable
-    DecPhase *d_dtable = nullptr;
-    unsigned *d_bar = nullptr;
-    unsigned long long *d_trace = nullptr;  // phase timestamps of the persistent kernel (tracing on)
     unsigned long long *d_gtrace = nullptr; // per-CTA timelines of batch-1 GEMV launches (tracing on)
     float *d_dbg = nullptr;                 // per-layer residual of the pass's last token (DebugLayer on)
     bool dbg_layers = false;
     int gtrace_slots = 0, gtrace_on = 0;
-    bool trace = false;
     int nchunks = 0;
     Pinned<int32_t> h_tok, h_seq, h_pos, h_out, h_topk, h_hist;
     Pinned<double> h_temp, h_topp;
@@ -655,138 +648,12 @@ int upload_sampler(acm_model *m, int ntok) {
     return ACM_OK;
 }
 
-// The persistent decode kernel is opt-in (ACM_MEGA=1): on the Qwen3-0.6B
-// shape it measures 790-820 tok/s against 938 for the multi-kernel graph.
-bool mega_enabled() {
-    static const bool on = [] {
-        const char *e = getenv("ACM_MEGA");
-        return e && e[0] == '1';
-    }();
-    return on;
-}
-
-// Build (once) the persistent decode kernel's phase table for batch 1.
-bool mega_ready(acm_model *m) {
-    if (m->dplan_state) return m->dplan_state > 0;
-    m->dplan_state = -1;
-    if (!mega_enabled() || m->kv_f16) return false;  // the persistent kernel reads an fp32 cache
-    const acm_config &c = m->c;
-    std::vector<DecLayerDesc> Ls(c.n_layers);
-    for (int l = 0; l < c.n_layers; l++) {
-        const Layer &L = m->layers[l];
-        DecLayerDesc &d = Ls[l];
-        d.q = L.q->d; d.k = L.k->d; d.v = L.v->d; d.o = L.o->d; d.gate = L.gate->d; d.up = L.up->d; d.down = L.down->d;
-        d.tq = (int)L.q->type; d.tk = (int)L.k->type; d.tv = (int)L.v->type; d.to = (int)L.o->type;
-        d.tg = (int)L.gate->type; d.tu = (int)L.up->type; d.td = (int)L.down->type;
-        d.attn_nw = L.attn_nw; d.ffn_nw = L.ffn_nw; d.q_nw = L.q_nw; d.k_nw = L.k_nw;
-        d.q_b = L.q_b; d.k_b = L.k_b; d.v_b = L.v_b;
-        d.x = m->x; d.q_out = m->q; d.k_out = m->k; d.v_out = m->v; d.att = m->att; d.hb = m->hb;
-    }
-    DecLmDesc lm{m->out->d, (int)m->out->type, m->out->rows(), m->out_nw, m->x, m->logits, c.vocab, m->d_seq,
-                 m->d_amax};
-    if (!decode_plan(m->dplan, Ls.data(), c.n_layers, lm, c.n_embd, c.n_head, c.n_head_kv, c.head_dim, c.n_ff,
-                     m->e->num_sms, 1))
-        return false;
-    if ((c.max_ctx + DEC_CHUNK - 1) / DEC_CHUNK > PART_TOKSPLIT) return false;
-    int coop = 0;
-    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->e->device);
-    if (!coop) return false;
-    if (decode_launch(m->dplan, nullptr, c.head_dim, m->e->stream) != cudaSuccess) {
-        cudaGetLastError();
-        return false;
-    }
-    if (dalloc(m, &m->d_dtable, m->dplan.table.size()) != cudaSuccess) return false;
-    if (cudaMemcpy(m->d_dtable, m->dplan.table.data(), sizeof(DecPhase) * m->dplan.table.size(),
-                   cudaMemcpyHostToDevice) != cudaSuccess)
-        return false;
-    if (dalloc(m, &m->d_bar, 4) != cudaSuccess) return false;
-    m->dplan_state = 1;
-    return true;
-}
-
-// Enqueue one batch-1 decode step on the persistent kernel.
-int mega_step(acm_model *m, bool greedy) {
-    const acm_config &c = m->c;
-    cudaStream_t st = m->e->stream;
-    const int hd = c.head_dim;
-    CK_M(cudaMemsetAsync(m->d_bar, 0, sizeof(unsigned), st));
-    CK_M(dequant_launch(m->embd->type, m->embd->d, c.n_embd, 1, m->d_tok, m->embd->rows(), m->x, c.n_embd, st));
-    DecArgs A{};
-    A.ph = m->d_dtable;
-    A.nph = m->dplan.nph;
-    A.ntok = 1;
-    A.eps = c.rms_eps;
-    A.ns = m->dplan.ns;
-    A.sb = m->dplan.sb;
-    A.ring_off = m->dplan.ring_off;
-    A.area_off = m->dplan.area_off;
-    A.meta_off = m->dplan.meta_off;
-    A.attn_group_floats = m->dplan.attn_group_floats;
-    A.part_rows = m->dplan.part_rows;
-    A.r = RopeDesc{m->q, m->k, m->v, nullptr, nullptr, m->rope_tab, c.n_head, c.n_head_kv, hd, c.rope_dim,
-                   c.rope_interleaved, c.rms_eps};
-    A.a = AttnDesc{m->q, m->att, c.n_head, c.n_head_kv, hd, 1.0f / (float)sqrt((double)hd), m->part,
-                   (c.max_ctx + DEC_CHUNK - 1) / DEC_CHUNK, m->d_attn_cnt, 0};
-    A.kv = KVDesc{m->kpool, m->vpool, m->d_page_table, m->max_pages, PAGE, m->layer_stride, c.n_head_kv * hd, 0};
-    A.tm = TokMeta{m->d_seq, m->d_pos};
-    A.bar = m->d_bar;
-    A.tok = m->d_tok;
-    A.pos = m->d_pos;
-    A.step = m->d_step;
-    A.out = m->d_out;
-    A.amax = greedy ? m->d_amax : nullptr;
-    A.hist = m->d_hist;
-    A.hist_ld = HIST_MAX;
-    A.hist_col = m->d_hist_col;
-    A.trace = m->trace ? m->d_trace : nullptr;
-    CK_M(decode_launch(m->dplan, &A, hd, st));
-    if (!greedy) {
-        CK_M(cudaMemsetAsync(m->d_amax, 0, sizeof(unsigned long long), st));
-        int rc = sample_pass(m, 1, false);
-        if (rc) return rc;
-        CK_M(advance_launch(m->d_tok, m->d_pos, m->d_step, m->d_out, nullptr, m->d_hist, HIST_MAX, m->d_hist_col, 1,
-                            st));
-    }
-    return ACM_OK;
-}
-
 // A decode step for `ntok` tokens: forward + sample + advance, replayed from
 // a CUDA graph captured on first use for this (batch size, greedy) pair.
-// Batch 1 runs on the persistent kernel when its plan fits the model.
 int decode_graph_launch(acm_model *m, int ntok, bool greedy) {
     const auto key = std::make_pair(ntok, greedy ? 1 : 0);
     auto it = m->graphs.find(key);
     cudaStream_t st = m->e->stream;
-    if (it == m->graphs.end() && ntok == 1 && mega_ready(m)) {
-        // warm-up outside capture (kernel attributes), then capture
-        int rc = mega_step(m, greedy);
-        if (rc) return rc;
-        CK_M(cudaMemsetAsync(m->d_amax, 0, sizeof(unsigned long long), st));
-        if ((rc = sync_check(m))) return rc;
-        // the warm-up advanced the device state; restore it from the staging
-        if ((rc = upload_meta(m, ntok))) return rc;
-        if ((rc = upload_sampler(m, ntok))) return rc;
-        CK_M(cudaMemsetAsync(m->d_hist_col, 0, sizeof(int32_t), st));
-        cudaGraph_t g = nullptr;
-        const unsigned long long before = g_kernel_launches.load();
-        CK_M(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-        rc = mega_step(m, greedy);
-        cudaError_t ce = cudaStreamEndCapture(st, &g);
-        const unsigned long long captured = g_kernel_launches.load() - before;
-        g_kernel_launches -= captured;
-        if (rc || ce != cudaSuccess) {
-            if (g) cudaGraphDestroy(g);
-            return rc ? rc : set_err(m, ACM_ERR_CUDA, fmt("graph capture failed: %s", cudaGetErrorString(ce)));
-        }
-        cudaGraphExec_t ex = nullptr;
-        cudaError_t ie = cudaGraphInstantiate(&ex, g, 0);
-        cudaGraphDestroy(g);
-        if (ie != cudaSuccess) return set_err(m, ACM_ERR_CUDA, fmt("graph instantiate: %s", cudaGetErrorString(ie)));
-        acm_model::Graph gr;
-        gr.exec = ex;
-        gr.kernels = captured;
-        it = m->graphs.emplace(key, gr).first;
-    }
     // greedy batches whose lm_head runs as a matvec fold the argmax into its
     // epilogue; larger batches (GEMM lm_head) take the greedy sampler pass
     const bool fold = greedy && gemv_supported((int)m->out->type, m->c.n_embd, ntok);
@@ -1821,33 +1688,6 @@ ACM_API int acm_model_last_timing(acm_model *m, double *prefill_s, double *decod
 
 ACM_API uint64_t acm_kernel_launches(void) { return g_kernel_launches.load(); }
 
-ACM_API int acm_model_trace(acm_model *m, int32_t enable) {
-    if (!m || !m->finalized) return set_err(m, ACM_ERR_INVALID, "model not finalized");
-    cudaSetDevice(m->e->device);
-    if (enable && !mega_ready(m)) return set_err(m, ACM_ERR_INVALID, "persistent decode kernel not available");
-    if (enable && !m->d_trace) {
-        CK_M(dalloc(m, &m->d_trace, (size_t)m->dplan.grid * m->dplan.nph * 4));
-        CK_M(cudaMemset(m->d_trace, 0, sizeof(unsigned long long) * m->dplan.grid * m->dplan.nph * 4));
-    }
-    if ((bool)enable != m->trace) {
-        m->trace = enable != 0;
-        // captured decode graphs bake the trace pointer in: rebuild them
-        for (auto &g : m->graphs) cudaGraphExecDestroy(g.second.exec);
-        m->graphs.clear();
-    }
-    return ACM_OK;
-}
-
-ACM_API int acm_model_trace_read(acm_model *m, uint64_t *out, int64_t cap, int32_t *nblocks, int32_t *nphases) {
-    if (!m || !m->trace || !m->d_trace || !out) return set_err(m, ACM_ERR_INVALID, "tracing not enabled");
-    const int64_t n = (int64_t)m->dplan.grid * m->dplan.nph * 4;
-    if (cap < n) return set_err(m, ACM_ERR_INVALID, "trace buffer too small");
-    cudaSetDevice(m->e->device);
-    CK_M(cudaMemcpy(out, m->d_trace, sizeof(uint64_t) * n, cudaMemcpyDeviceToHost));
-    if (nblocks) *nblocks = m->dplan.grid;
-    if (nphases) *nphases = m->dplan.nph;
-    return ACM_OK;
-}
 
 ACM_API int acm_model_debug_layers(acm_model *m, int32_t enable) {
     if (!m || !m->finalized) return set_err(m, ACM_ERR_INVALID, "model not finalized");

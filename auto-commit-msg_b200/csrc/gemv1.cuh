@@ -17,9 +17,8 @@
 //     two-lane fp32 (FADD2 / FFMA2), a shuffle reduction per row, and the
 //     epilogues (store + bias, residual add, SwiGLU of a gate/up pair, greedy
 //     argmax key).
-// Two users: k_gemv1.cu (one launch per matvec; each team moves its rows into
-// its own stages with the bulk-copy engine before the dependency wait) and
-// the persistent decode kernel (rows streamed through a shared ring).
+// User: k_gemv1.cu (one launch per matvec; each team moves its rows into its
+// own stages with the bulk-copy engine before the dependency wait).
 #pragma once
 #include "common.cuh"
 #include "gemv_dev.cuh"
@@ -736,62 +735,6 @@ __device__ __forceinline__ void gemv1_rows(const Gemv1Args &a, const GemvSeg &s,
     }
     trace_stamp(a.trace, 5);
     flush_best(c);
-}
-
-// ---------------------------------------------------------------------------
-// Persistent decode kernel: the rows of one phase streamed through a shared
-// ring; stage i of the phase is ring slot (cur + i) % ns, filled by the
-// producer warp and freed by every one of the ncw consumer warps arriving on
-// its empty barrier.  Rows of a stage go to the teams round robin (team t:
-// rows r0 + t, r0 + t + nteams, ...).  part: nteams x (part_rows * 2 * ts +
-// ts) floats; abort: the CTA's abort flag (a timed-out wait makes every
-// consumer warp leave).  Returns false on abort.
-// ---------------------------------------------------------------------------
-template <int T>
-__device__ __forceinline__ bool gemv1_ring(const GemvSeg &s, int r0, int r1, int K, uint64_t *full, uint64_t *empty,
-                                           const uint8_t *stg, int ns, int sb, uint32_t cur, const float *xs,
-                                           float *part, int part_rows, int ncw, int *abort,
-                                           unsigned long long *tp = nullptr) {
-    constexpr int NC = lane_elems<T>() / 4;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const RowGeo geo = row_geo(T, K);
-    const int TS = geo.ts, NT = ncw / TS;
-    const int team = warp / TS, tw = warp - team * TS;
-    const bool active = team < NT;
-    float *tpart = part + (size_t)team * (part_rows * 2 * TS + TS);
-    RowCtx c;
-    XRegN<NC> xr;
-    float2 xsm;
-    lane_setup<T, NC>(c, s, xs, geo, tw, r0 + team, NT, active ? (r1 - r0 - team + NT - 1) / NT : 0, xr, xsm);
-    c.res_step = 1;
-    const int R = s.rows_per_stage, nst = (r1 - r0 + R - 1) / R;
-    for (int i = 0; i < nst; i++) {
-        const uint32_t ring = cur + (uint32_t)i;
-        const int slot = (int)(ring % (uint32_t)ns);
-        if (!mbar_wait(&full[slot], (ring / (uint32_t)ns) & 1u) && lane == 0) *abort = 1;
-        named_sync(1, ncw * 32);
-        if (*(volatile int *)abort) return false;
-        if (i == 0 && tp && threadIdx.x == 0) {
-            unsigned long long t;
-            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-            tp[2] = t;
-        }
-        const int ra = r0 + i * R, rbn = min(ra + R, r1);
-        const int64_t a0 = ((int64_t)ra * s.rb) & ~int64_t(15);
-        const int64_t a1 = ((int64_t)rbn * s.rb + 15) & ~int64_t(15);
-        const int64_t c0 = ((int64_t)ra * s.rb2) & ~int64_t(15);
-        const uint8_t *buf = stg + (size_t)slot * sb;
-        // this team's first row of the stage (team-wide index continues over stages)
-        const int first = ra + ((team - (ra - r0) % NT) % NT + NT) % NT;
-        const int cnt = first < rbn ? (rbn - first + NT - 1) / NT : 0;
-        if (active)
-            stage_rows<T, NC>(c, geo, K, buf, a0, buf + (a1 - a0), c0, first, NT, cnt, (first - r0 - team) / NT, tw,
-                              6 + team, tpart, xr, xsm);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-    }
-    if (active) flush_best(c);
-    return true;
 }
 
 }  // namespace acm

@@ -1,8 +1,7 @@
-// gemv_dev.cuh -- device side of the fused dequant-GEMV (see k_gemv.cu),
-// shared by the per-launch GEMV kernel and the persistent decode kernel.
-// A CTA consumes the stages of its row range from a ring of shared-memory
-// stages; `cur` is the ring position of the range's first stage (0 for a
-// single GEMV launch, running across phases in the persistent kernel).
+// gemv_dev.cuh -- device side of the fused dequant-GEMV of k_gemv.cu (the
+// lm_head and matvecs of 2..8 tokens).  A CTA consumes the stages of its row
+// range from a ring of shared-memory stages; `cur` is the ring position of
+// the range's first stage (0 for a single GEMV launch).
 #pragma once
 #include "common.cuh"
 #include "kernels.h"

@@ -267,67 +267,6 @@ cudaError_t sample_launch(const SampleDesc &s, int ntok, bool all_greedy, cudaSt
 cudaError_t advance_launch(int32_t *tok, int32_t *pos, uint64_t *step, int32_t *out, unsigned long long *amax,
                            int32_t *hist, int hist_ld, int32_t *hist_col, int ntok, cudaStream_t st);
 
-// ---------------------------------------------------------------------------
-// Persistent decode kernel (k_decode.cu): one cooperative launch per decode
-// step.  The host builds a per-CTA table of phases (GEMV row ranges and
-// attention phases) once per model.
-enum : int { DPH_GEMV = 0, DPH_ATTN = 1 };
-struct DecPhase {
-    int kind, layer;
-    const float *x;          // GEMV input activations
-    int ldx, k, lpr, pad_;
-    const float *norm_w;     // optional RMSNorm weight of the input
-    GemvSeg seg;             // this CTA's matrix segment
-    int r0, r1;              // this CTA's rows
-    const float *q_nw, *k_nw;  // attention: QK-norm weights of the layer
-};
-struct DecArgs {
-    const DecPhase *ph;      // [grid][nph]
-    int nph, ntok;
-    float eps;
-    int ns, sb, ring_off, area_off, meta_off, attn_group_floats;
-    int part_rows;           // GEMV team partial rows per stage
-    RopeDesc r;
-    AttnDesc a;
-    KVDesc kv;
-    TokMeta tm;
-    unsigned *bar;           // grid barrier counter, zeroed before each launch
-    int32_t *tok, *pos;
-    uint64_t *step;
-    int32_t *out;
-    unsigned long long *amax;  // greedy: argmax keys; null = leave sampling to later kernels
-    int32_t *hist;
-    int hist_ld;
-    int32_t *hist_col;
-    unsigned long long *trace;  // optional [grid][nph][2] globaltimer: phase start, barrier arrival
-};
-struct DecLayerDesc {
-    const void *q, *k, *v, *o, *gate, *up, *down;
-    int tq, tk, tv, to, tg, tu, td;
-    const float *attn_nw, *ffn_nw, *q_nw, *k_nw, *q_b, *k_b, *v_b;
-    float *x, *q_out, *k_out, *v_out, *att, *hb;
-};
-struct DecLmDesc {
-    const void *w;
-    int type;
-    int64_t rows;
-    const float *norm_w, *x;
-    float *logits;
-    int ldy;
-    const int32_t *yrow;
-    unsigned long long *amax;
-};
-struct DecPlan {
-    int inst = 0, grid = 0, nph = 0, ns = 0, sb = 0, ring_off = 0, area_off = 0, meta_off = 0, attn_group_floats = 0;
-    int part_rows = 1;
-    size_t smem = 0;
-    std::vector<DecPhase> table;
-};
-bool decode_plan(DecPlan &plan, const DecLayerDesc *layers, int n_layers, const DecLmDesc &lm, int n_embd,
-                 int n_head, int n_head_kv, int head_dim, int n_ff, int num_sms, int ntok);
-// A == nullptr: only check that the instance's CTA fits on an SM.
-cudaError_t decode_launch(const DecPlan &plan, const DecArgs *A, int head_dim, cudaStream_t st);
-constexpr int DEC_CHUNK = 16;  // attention chunk of the persistent kernel (positions)
 
 // Device error flag (timeouts in bounded waits).
 int read_and_clear_dev_error();

@@ -477,9 +477,7 @@ def run_kernels(args, rank, world, local):
 
 def run_profile(args):
     """Short workloads for the profiler (no JSON line): `prefill` runs three
-    389-token prefills; `decode` one prefill + `--tokens` greedy decode tokens;
-    `trace` the same with the persistent decode kernel's per-phase timestamps
-    (acm_model_trace) and prints per-phase-kind spans of the last token."""
+    389-token prefills; `decode` one prefill + `--tokens` greedy decode tokens."""
     import ctypes as C
 
     import numpy as np
@@ -574,35 +572,8 @@ def run_profile(args):
             print(f"prefill {i}: {1e3 * m.last_timing()[0]:.3f} ms", flush=True)
             m.Reset()
     else:
-        if args.profile == "trace":
-            rc = lib.acm_model_trace(m.handle, 1)
-            if rc:
-                print("trace unavailable:", lib.acm_last_error(m.handle).decode())
-                args.profile = "decode"
         ids = m.Generate(prompt, acm.Sampler(0.0), args.tokens, stop_on_eos=False)
         print(f"decode {args.tokens} tokens: {args.tokens / m.Stats.Decode:.1f} tok/s", flush=True)
-        if args.profile == "trace":
-            cap = 148 * 1024 * 4
-            buf = (C.c_uint64 * cap)()
-            nb, nph = C.c_int32(), C.c_int32()
-            if lib.acm_model_trace_read(m.handle, buf, cap, C.byref(nb), C.byref(nph)) == 0:
-                nb, nph = nb.value, nph.value
-                t = np.frombuffer(buf, dtype=np.uint64)[: nb * nph * 4].reshape(nb, nph, 4).astype(np.int64)
-                t0 = t[:, 0, 0].min()
-                kinds = ["qkv", "attn", "o", "ffn", "down"]
-                print(f"persistent kernel: {nb} CTAs, {nph} phases, token {(t[:, -1, 3].max() - t0) / 1e3:.1f} us")
-                for ki, kname in enumerate(kinds + ["lm_head"]):
-                    ps = [nph - 1] if kname == "lm_head" else list(range(ki, nph - 1, 5))
-                    span = [(t[:, p, 3].max() - t[:, p, 0].min()) / 1e3 for p in ps]
-                    work = [float(np.median(t[:, p, 3] - t[:, p, 0])) / 1e3 for p in ps]
-                    line = f"  {kname:8s} phases {len(ps):3d}  span {np.mean(span):7.2f} us  median CTA work {np.mean(work):6.2f} us"
-                    st = [p for p in ps if (t[:, p, 1] > 0).all()]
-                    if st:
-                        stage = np.mean([float(np.median(t[:, p, 1] - t[:, p, 0])) for p in st]) / 1e3
-                        wts = np.mean([float(np.median(t[:, p, 2] - t[:, p, 1])) for p in st if (t[:, p, 2] > 0).all()] or [0]) / 1e3
-                        rows = np.mean([float(np.median(t[:, p, 3] - np.maximum(t[:, p, 2], t[:, p, 1]))) for p in st]) / 1e3
-                        line += f"  (staged {stage:5.2f}, weights +{wts:5.2f}, rows {rows:5.2f})"
-                    print(line)
     m.close()
     eng.close()
 
@@ -614,14 +585,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--profile", choices=["prefill", "decode", "trace", "gtrace", "load", "gemv", "serve"],
+    ap.add_argument("--profile", choices=["prefill", "decode", "gtrace", "load", "gemv", "serve"],
                     help="run a short workload for the profiler instead of the benchmark")
-    ap.add_argument("--tokens", type=int, default=8, help="decode tokens of --profile decode/trace")
+    ap.add_argument("--tokens", type=int, default=8, help="decode tokens of --profile decode/gtrace")
     ap.add_argument("--type", choices=list(KB_TYPES), default="q4_k", help="weight type of --profile gemv")
     ap.add_argument("--kv-f16", action="store_true",
                     help="--workload serve / --profile serve with the reduced-precision (IEEE half) KV cache")
     ap.add_argument("--model", choices=list(MODELS), default="qwen3",
-                    help="model shape of --profile prefill/decode/trace/load (qwen3: the benchmark's own)")
+                    help="model shape of --profile prefill/decode/gtrace/load (qwen3: the benchmark's own)")
     ap.add_argument("--workload", choices=["single", "serve", "kernels"], default="single",
                     help="single: the batch-1 Generate benchmark (default); serve: 512 requests through acm_serve; "
                          "kernels: the matmul microbench over every quantized type and weight shape")

@@ -98,8 +98,7 @@ ACM_API const char *acm_engine_error(acm_engine *e);
  * (the appended position is rounded before its own step uses it, so a
  * position reads the same values in every step).  Logits then differ from
  * the reference's fp32 path by more than rounding order; the measured
- * deviation is stated with the tests that check it.  The persistent decode
- * kernel (ACM_MEGA=1) is not used for such models.  Default: fp32. */
+ * deviation is stated with the tests that check it.  Default: fp32. */
 ACM_API int acm_engine_set_kv_f16(acm_engine *e, int32_t enable);
 
 /* Failure detection, no reference counterpart.  Every device-side wait of
@@ -288,16 +287,6 @@ ACM_API int acm_model_last_timing(acm_model *m, double *prefill_s, double *decod
  * replay counts every kernel the graph holds).  No reference counterpart. */
 ACM_API uint64_t acm_kernel_launches(void);
 
-/* Tracing, no reference counterpart (the reference's only tracing is its
- * Stats wall clock, sampler.go:101-106): when enabled, batch-1 decode steps
- * on the persistent decode kernel record, per CTA and phase (q/k/v,
- * attention, o, gate/up, down per layer, then lm_head), the %globaltimer ns at
- * which the CTA started the phase, had staged its activations and had its
- * first weights stage (GEMV phases; 0 otherwise), and arrived at the
- * following barrier.  acm_model_trace_read copies the last step's
- * [nblocks][nphases][4] values. */
-ACM_API int acm_model_trace(acm_model *m, int32_t enable);
-ACM_API int acm_model_trace_read(acm_model *m, uint64_t *out, int64_t cap, int32_t *nblocks, int32_t *nphases);
 /* DebugLayer (model.go:231-233, called at :427-429 after each layer's
  * residual update): with enable != 0, every pass from now on (prefill chunks
  * and decode steps; decode graphs are rebuilt) copies the residual stream x
