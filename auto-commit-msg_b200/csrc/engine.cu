@@ -319,11 +319,14 @@ bool mma_ready(acm_model *m) {
 
 // Split fp32 activations x [ntok][k] into the model's bf16 buffers and
 // return the maps for this K (nullptr when the tensor-core path is off).
-int mma_split_x(acm_model *m, const float *x, int ldx, int ntok, int k, const TensorMap **hi, const TensorMap **lo) {
+// norm_w: RMSNorm the rows first (one fused launch).
+int mma_split_x(acm_model *m, const float *x, int ldx, int ntok, int k, const TensorMap **hi, const TensorMap **lo,
+                const float *norm_w = nullptr, float eps = 0.f) {
     int i = 0;
     while (i < 3 && m->xmap_k[i] != k) i++;
     if (i == 3) return set_err(m, ACM_ERR_INVALID, "no activation map for this K");
-    CK_M(split_act_launch(x, ldx, ntok, k, m->xs_hi, m->xs_lo, m->e->stream));
+    if (norm_w) CK_M(split_act_norm_launch(x, ldx, ntok, k, norm_w, eps, m->xs_hi, m->xs_lo, m->e->stream));
+    else CK_M(split_act_launch(x, ldx, ntok, k, m->xs_hi, m->xs_lo, m->e->stream));
     *hi = &m->xmap_hi[i];
     *lo = &m->xmap_lo[i];
     return ACM_OK;
@@ -490,9 +493,8 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
             CK_M(gemv_launch(sg, 3, m->x, E, E, ntok, L.attn_nw, eps, S, st, pf_o, 1));
         } else if (use_mma_dq(m, {L.q, L.k, L.v}, E) || use_mma(m, {L.q, L.k, L.v})) {
             const bool dq = use_mma_dq(m, {L.q, L.k, L.v}, E);
-            CK_M(rmsnorm_launch(m->x, E, L.attn_nw, m->h, E, ntok, E, eps, st));
             const TensorMap *xh, *xl;
-            if (int rc = mma_split_x(m, m->h, E, ntok, E, &xh, &xl)) return rc;
+            if (int rc = mma_split_x(m, m->x, E, ntok, E, &xh, &xl, L.attn_nw, eps)) return rc;
             MmaGemmSeg sg[3] = {{&L.q->mhi, &L.q->mlo, nullptr, nullptr, qd, EPI_STORE, m->q, qd, L.q_b, nullptr,
                                  L.q->d, nullptr, dq ? (int)L.q->type : -1},
                                 {&L.k->mhi, &L.k->mlo, nullptr, nullptr, kvd, EPI_STORE, m->k, kvd, L.k_b, nullptr,
@@ -554,9 +556,8 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
             // one paired launch: both projections dequantized in the kernel
             // (same type), else both split to bf16 whatever their types
             const bool dq = pair && use_mma_dq(m, {L.gate, L.up}, E);
-            CK_M(rmsnorm_launch(m->x, E, L.ffn_nw, m->h, E, ntok, E, eps, st));
             const TensorMap *xh, *xl;
-            if (int rc = mma_split_x(m, m->h, E, ntok, E, &xh, &xl)) return rc;
+            if (int rc = mma_split_x(m, m->x, E, ntok, E, &xh, &xl, L.ffn_nw, eps)) return rc;
             MmaGemmSeg sf{&L.gate->mhi, &L.gate->mlo, &L.up->mhi, &L.up->mlo, F, EPI_SWIGLU, m->hb, F, nullptr, nullptr,
                           L.gate->d, L.up->d, dq ? (int)L.gate->type : -1};
             CK_M(mma_run(&sf, 1, xh, xl, ntok, E, st));

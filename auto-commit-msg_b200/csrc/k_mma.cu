@@ -339,6 +339,39 @@ __global__ void k_split_act(const float *x, int ldx, int m, int k, __nv_bfloat16
     }
 }
 
+// RMSNorm (model.go:213-222) of row blockIdx.x fused with its split: the
+// same arithmetic and reduction order as k_rmsnorm (k_misc.cu), so the split
+// values are those of rmsnorm followed by k_split_act.  256 threads per row.
+__global__ void __launch_bounds__(256) k_split_act_norm(const float *x, int ldx, int k, const float *w, float eps,
+                                                        __nv_bfloat16 *hi, __nv_bfloat16 *lo) {
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
+    __shared__ float red[8];
+    const int r = blockIdx.x;
+    const float *xr = x + (int64_t)r * ldx;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < k; i += 256) ss = fmaf(xr[i], xr[i], ss);
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) t += red[i];
+    const float sc = rms_scale(t, k, eps);
+    for (int c = threadIdx.x * 4; c < k; c += 1024) {
+        const float4 v = *reinterpret_cast<const float4 *>(xr + c);
+        const float4 g = *reinterpret_cast<const float4 *>(w + c);
+        __nv_bfloat16 h[4], l[4];
+        split_bf16(__fmul_rn(__fmul_rn(v.x, sc), g.x), h[0], l[0]);
+        split_bf16(__fmul_rn(__fmul_rn(v.y, sc), g.y), h[1], l[1]);
+        split_bf16(__fmul_rn(__fmul_rn(v.z, sc), g.z), h[2], l[2]);
+        split_bf16(__fmul_rn(__fmul_rn(v.w, sc), g.w), h[3], l[3]);
+        const int64_t e = blk64(r, c, k);
+        *reinterpret_cast<uint2 *>(hi + e) = *reinterpret_cast<uint2 *>(h);
+        *reinterpret_cast<uint2 *>(lo + e) = *reinterpret_cast<uint2 *>(l);
+    }
+}
+
 // Exact dequantization of W [n][k] (ggml blocks) -> hi, lo bf16, 64x64-blocked.
 template <int T>
 __global__ void k_split_weight(const uint8_t *w, int64_t n, int k, __nv_bfloat16 *hi, __nv_bfloat16 *lo) {
@@ -526,6 +559,16 @@ cudaError_t split_act_launch(const float *x, int ldx, int m, int k, void *hi, vo
     const int64_t total = (int64_t)m * k / 4;
     const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
     cudaError_t e = launch_pdl(k_split_act, dim3(grid), dim3(256), 0, st, x, ldx, m, k,
+                               static_cast<__nv_bfloat16 *>(hi), static_cast<__nv_bfloat16 *>(lo));
+    if (e != cudaSuccess) return e;
+    return launched(1);
+}
+
+cudaError_t split_act_norm_launch(const float *x, int ldx, int m, int k, const float *norm_w, float eps, void *hi,
+                                  void *lo, cudaStream_t st) {
+    if (m <= 0) return cudaSuccess;
+    if (k % 4 || ldx % 4 || !norm_w || ((uintptr_t)x & 15) || ((uintptr_t)norm_w & 15)) return cudaErrorInvalidValue;
+    cudaError_t e = launch_pdl(k_split_act_norm, dim3(m), dim3(256), 0, st, x, ldx, k, norm_w, eps,
                                static_cast<__nv_bfloat16 *>(hi), static_cast<__nv_bfloat16 *>(lo));
     if (e != cudaSuccess) return e;
     return launched(1);

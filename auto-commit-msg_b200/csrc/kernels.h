@@ -113,6 +113,9 @@ bool bf16_map(TensorMap *map, const void *base, int64_t rows, int64_t k);
 inline int64_t rows64(int64_t rows) { return (rows + 63) / 64 * 64; }
 // fp32 [m][ldx] -> bf16 hi, lo (blocked)
 cudaError_t split_act_launch(const float *x, int ldx, int m, int k, void *hi, void *lo, cudaStream_t st);
+// RMSNorm of each row (weight norm_w) and its split in one launch
+cudaError_t split_act_norm_launch(const float *x, int ldx, int m, int k, const float *norm_w, float eps, void *hi,
+                                  void *lo, cudaStream_t st);
 // exact dequant of W [n][k] -> bf16 hi, lo (blocked)
 cudaError_t split_weight_launch(int type, const void *w, int64_t n, int k, void *hi, void *lo, cudaStream_t st);
 struct MmaGemmSeg {
