@@ -15,6 +15,7 @@
 #include <stdlib.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "attn_dev.cuh"
 #include "common.cuh"
@@ -444,7 +445,7 @@ static cudaError_t launch_tiled(const RopeDesc &r, const AttnDesc &a, const KVDe
                                int ntok, int nsplit, cudaStream_t st) {
     const int G = a.n_head / a.n_head_kv;
     const size_t smem = (size_t)tiled_smem_floats(HD, G, (int)sizeof(KT)) * sizeof(float);
-    static bool attr[64] = {};
+    static std::atomic<bool> attr[64] = {};  // per device: attributes set (host threads may race)
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr[dev & 63]) {
@@ -667,7 +668,7 @@ cudaError_t attention_prefill_launch(const AttnDesc &a, const KVDesc &kv, int la
     if ((R / 4) * 8 > 256 && R > 128) return cudaErrorInvalidValue;
     const int QS = HD + 4;
     const size_t smem = ((size_t)R * QS + PKT * QS + PKT * HD + (size_t)R * (PKT + 1) + 2 * R) * sizeof(float);
-    static bool attr[64][2] = {};
+    static std::atomic<bool> attr[64][2] = {};  // per device and variant: attributes set
     int dev = 0;
     cudaGetDevice(&dev);
     const int hi = HD == 128 ? 0 : 1;
@@ -695,7 +696,7 @@ cudaError_t attention_launch(const AttnDesc &a, const KVDesc &kv, int layer, Tok
     const size_t smem = ((size_t)G * HD + (size_t)G * chunk_max + 2 * G + red) * sizeof(float);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     dim3 grid(ntok, a.n_head_kv, a.nsplit);
-    static bool attr[64][2] = {};
+    static std::atomic<bool> attr[64][2] = {};  // per device and variant: attributes set
     int dev = 0;
     cudaGetDevice(&dev);
     if (HD == 128) {

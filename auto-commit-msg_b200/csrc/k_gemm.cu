@@ -7,6 +7,7 @@
 // the other half stages the activation tile; then every thread accumulates a
 // 4x4 register tile.  A SwiGLU pair decodes both gate and up tiles.
 #include <algorithm>
+#include <atomic>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -135,7 +136,7 @@ cudaError_t gemm_launch(const GemmDesc &d, cudaStream_t st) {
     if (pair != (d.epi == EPI_SWIGLU)) return cudaErrorInvalidValue;
     dim3 grid((unsigned)((d.n + GB - 1) / GB), (unsigned)((d.m + GB - 1) / GB));
     const size_t smem = (size_t)(pair ? 3 : 2) * GK * (GB + GPAD) * sizeof(float);
-    static bool attr[64] = {};
+    static std::atomic<bool> attr[64] = {};  // per device: attributes set (host threads may race)
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr[dev & 63]) {

@@ -23,6 +23,7 @@
 #include <stdlib.h>
 
 #include <algorithm>
+#include <atomic>
 #include <vector>
 
 #include "common.cuh"
@@ -150,7 +151,7 @@ static bool sb_ok(int type) {
 
 template <int MT, int TA, int TB>
 static cudaError_t launch_one(GemvArgs &a, int grid, size_t smem, cudaStream_t st) {
-    static bool attr_done[64] = {};
+    static std::atomic<bool> attr_done[64] = {};  // per device: attributes set (host threads may race)
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr_done[dev & 63]) {

@@ -11,6 +11,7 @@
 #include <stdlib.h>
 
 #include <algorithm>
+#include <atomic>
 #include <vector>
 
 #include "common.cuh"
@@ -120,7 +121,7 @@ bool gemv1_supported(int type, int64_t k) {
 
 template <int TA, int TB>
 static cudaError_t launch_inst(const Gemv1Args &a, int grid, int nthreads, size_t smem, cudaStream_t st) {
-    static bool attr_done[64] = {};
+    static std::atomic<bool> attr_done[64] = {};  // per device: attributes set (host threads may race)
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr_done[dev & 63]) {

@@ -5,6 +5,8 @@
 //   top-k / greedy sampler            (sampler.go:19-98)
 #include <float.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "launch.cuh"
@@ -412,7 +414,7 @@ cudaError_t sample_launch(const SampleDesc &d, int ntok, bool all_greedy, cudaSt
     while (np < d.nchunks * kk) np <<= 1;
     // keys, the top-64 gather buffer, histogram and control words
     const size_t smem = kk > 1 ? 2 * (size_t)np * sizeof(uint64_t) + 256 * 4 + 16 : (size_t)np * sizeof(uint64_t);
-    static bool attr[64] = {};
+    static std::atomic<bool> attr[64] = {};  // per device: attributes set (host threads may race)
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr[dev & 63]) {

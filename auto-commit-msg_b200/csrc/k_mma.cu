@@ -33,6 +33,7 @@
 // Every wait is bounded; on a timeout the kernel records DEV_ERR_TIMEOUT,
 // waits (bounded) for its copies and MMAs in flight, frees TMEM and returns.
 #include <cuda.h>
+#include <atomic>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <float.h>
@@ -665,7 +666,7 @@ cudaError_t mma_gemm_batched_launch(const MmaGemmSeg *segs, int nseg, const Tens
         const int rpt = s.pair ? MBM / 2 : MBM;
         tiles += (int)((g.n + rpt - 1) / rpt) * a.ttiles;
     }
-    static bool attr[64] = {};
+    static std::atomic<bool> attr[64] = {};  // per device: attributes set (host threads may race)
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr[dev & 63]) {

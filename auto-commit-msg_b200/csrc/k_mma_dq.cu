@@ -27,6 +27,7 @@
 // bytes (4.6 KB for Q4_K) and 32 KB of activation splits, against 48 KB of
 // split operands for half the tokens in k_mma.cu.  No cluster multicast.
 #include <cuda.h>
+#include <atomic>
 #include <cuda_bf16.h>
 #include <float.h>
 #include <string.h>
@@ -462,7 +463,7 @@ static int num_sms() {
 
 template <int TA, int TB>
 static cudaError_t dq_inst(const DqArgs &a, dim3 grid, size_t smem, cudaStream_t st) {
-    static bool attr[64] = {};
+    static std::atomic<bool> attr[64] = {};  // per device: attributes set (host threads may race)
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr[dev & 63]) {
