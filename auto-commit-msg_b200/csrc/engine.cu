@@ -448,8 +448,9 @@ bool use_mma_dq(acm_model *m, std::initializer_list<DevTensor *> ts, int64_t k) 
 // Launch a tensor-core GEMM: weights dequantized in the kernel when the
 // segments carry GGUF rows (wtype >= 0), else from their split caches.
 cudaError_t mma_run(const MmaGemmSeg *segs, int nseg, const TensorMap *xh, const TensorMap *xl, int m, int k,
-                    cudaStream_t st, float *ws = nullptr, size_t wsf = 0) {
-    if (segs[0].wtype >= 0) return mma_dq_launch(segs, nseg, xh, xl, m, k, st, ws, wsf);
+                    cudaStream_t st, float *ws = nullptr, size_t wsf = 0, int *defer_ks = nullptr) {
+    if (defer_ks) *defer_ks = 0;
+    if (segs[0].wtype >= 0) return mma_dq_launch(segs, nseg, xh, xl, m, k, st, ws, wsf, defer_ks);
     return mma_gemm_launch(segs, nseg, xh, xl, m, k, st, ws, wsf);
 }
 
@@ -524,6 +525,12 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
                 CK_M(attention_prefill_launch(ad, kv, l, tm, ntok, st));
             }
         }
+        // the gate/up GEMM on the tensor cores (its RMSNorm fused into the
+        // activations' split, and then the o GEMM's split-K reduce too)
+        const bool pair = L.gate->type == L.up->type;
+        const bool gu_mma = !(gemv_supported(L.gate->type, E, ntok) && gemv_supported(L.up->type, E, ntok)) &&
+                            F % 64 == 0 && ((pair && use_mma_dq(m, {L.gate, L.up}, E)) || use_mma(m, {L.gate, L.up}));
+        int o_ks = 0;  // split-K slices of the o GEMM left for the gate/up staging to reduce
         // x += Wo att
         if (gemv_supported(L.o->type, qd, ntok)) {
             GemvSegDesc so{L.o->d, nullptr, (int)L.o->type, E, EPI_ADD, m->x, E, nullptr, nullptr};
@@ -535,13 +542,12 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
             if (int rc = mma_split_x(m, m->att, qd, ntok, qd, &xh, &xl)) return rc;
             MmaGemmSeg so{&L.o->mhi, &L.o->mlo, nullptr, nullptr, E, EPI_ADD, m->x, E, nullptr, nullptr,
                           L.o->d, nullptr, dq ? (int)L.o->type : -1};
-            CK_M(mma_run(&so, 1, xh, xl, ntok, qd, st, m->mma_ws, m->mma_ws_floats));
+            CK_M(mma_run(&so, 1, xh, xl, ntok, qd, st, m->mma_ws, m->mma_ws_floats, gu_mma ? &o_ks : nullptr));
         } else {
             CK_M(gemm_launch({L.o->d, nullptr, (int)L.o->type, E, qd, ntok, m->att, qd, m->x, E, EPI_ADD, nullptr, nullptr}, st));
         }
         // hb = silu(Wg h) * (Wu h), h = RMSNorm(x)
-        const bool pair = L.gate->type == L.up->type;
-        if (gemv_supported(L.gate->type, E, ntok) && gemv_supported(L.up->type, E, ntok)) {
+        if (!gu_mma && gemv_supported(L.gate->type, E, ntok) && gemv_supported(L.up->type, E, ntok)) {
             if (pair) {
                 GemvSegDesc sf{L.gate->d, L.up->d, (int)L.gate->type, F, EPI_SWIGLU, m->hb, F, nullptr, nullptr};
                 const L2Range pf_d[1] = {{L.down->d, (int64_t)L.down->nbytes}};
@@ -552,12 +558,23 @@ int forward_pass(acm_model *m, int ntok, int max_pos, int lm_first, int lm_count
                 CK_M(gemv_launch(sf, 2, m->x, E, E, ntok, L.ffn_nw, eps, S, st));
                 CK_M(swiglu_launch(m->hb, m->hb2, m->hb, (int64_t)ntok * F, st));
             }
-        } else if (F % 64 == 0 && ((pair && use_mma_dq(m, {L.gate, L.up}, E)) || use_mma(m, {L.gate, L.up}))) {
+        } else if (gu_mma) {
             // one paired launch: both projections dequantized in the kernel
             // (same type), else both split to bf16 whatever their types
             const bool dq = pair && use_mma_dq(m, {L.gate, L.up}, E);
             const TensorMap *xh, *xl;
-            if (int rc = mma_split_x(m, m->x, E, ntok, E, &xh, &xl, L.ffn_nw, eps)) return rc;
+            if (o_ks > 0) {
+                // x += the o GEMM's partial sums, RMSNorm, split: one launch
+                int i = 0;
+                while (i < 3 && m->xmap_k[i] != E) i++;
+                if (i == 3) return set_err(m, ACM_ERR_INVALID, "no activation map for this K");
+                CK_M(split_act_reduce_norm_launch(m->mma_ws, o_ks, ntok, m->x, E, L.ffn_nw, eps, m->xs_hi, m->xs_lo,
+                                                  st));
+                xh = &m->xmap_hi[i];
+                xl = &m->xmap_lo[i];
+            } else if (int rc = mma_split_x(m, m->x, E, ntok, E, &xh, &xl, L.ffn_nw, eps)) {
+                return rc;
+            }
             MmaGemmSeg sf{&L.gate->mhi, &L.gate->mlo, &L.up->mhi, &L.up->mlo, F, EPI_SWIGLU, m->hb, F, nullptr, nullptr,
                           L.gate->d, L.up->d, dq ? (int)L.gate->type : -1};
             CK_M(mma_run(&sf, 1, xh, xl, ntok, E, st));

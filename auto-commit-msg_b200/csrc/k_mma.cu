@@ -373,6 +373,60 @@ __global__ void __launch_bounds__(256) k_split_act_norm(const float *x, int ldx,
     }
 }
 
+// A split-K GEMM's residual add (x += the ks partial sums of ws, in order, as
+// k_split_reduce) fused with the RMSNorm and split of the resulting rows that
+// the next GEMM reads (as k_split_act_norm): one launch instead of two, the
+// same values.  Row blockIdx.x, 256 threads.
+__global__ void __launch_bounds__(256) k_split_act_reduce_norm(const float *ws, int ks, int m, float *x, int k,
+                                                               const float *w, float eps, __nv_bfloat16 *hi,
+                                                               __nv_bfloat16 *lo) {
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
+    __shared__ float red[8];
+    const int r = blockIdx.x;
+    float *xr = x + (int64_t)r * k;
+    const int64_t total = (int64_t)m * k;
+    for (int c = threadIdx.x * 4; c < k; c += 1024) {
+        const int64_t i = (int64_t)r * k + c;
+        float4 v = *reinterpret_cast<const float4 *>(ws + i);
+        for (int s = 1; s < ks; s++) {
+            const float4 p = *reinterpret_cast<const float4 *>(ws + (int64_t)s * total + i);
+            v.x += p.x;
+            v.y += p.y;
+            v.z += p.z;
+            v.w += p.w;
+        }
+        float4 y = *reinterpret_cast<const float4 *>(xr + c);
+        y.x = y.x + v.x;
+        y.y = y.y + v.y;
+        y.z = y.z + v.z;
+        y.w = y.w + v.w;
+        *reinterpret_cast<float4 *>(xr + c) = y;
+    }
+    __syncthreads();  // the row's new values, written by other threads of the CTA
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < k; i += 256) ss = fmaf(xr[i], xr[i], ss);
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) t += red[i];
+    const float sc = rms_scale(t, k, eps);
+    for (int c = threadIdx.x * 4; c < k; c += 1024) {
+        const float4 v = *reinterpret_cast<const float4 *>(xr + c);
+        const float4 g = *reinterpret_cast<const float4 *>(w + c);
+        __nv_bfloat16 h[4], l[4];
+        split_bf16(__fmul_rn(__fmul_rn(v.x, sc), g.x), h[0], l[0]);
+        split_bf16(__fmul_rn(__fmul_rn(v.y, sc), g.y), h[1], l[1]);
+        split_bf16(__fmul_rn(__fmul_rn(v.z, sc), g.z), h[2], l[2]);
+        split_bf16(__fmul_rn(__fmul_rn(v.w, sc), g.w), h[3], l[3]);
+        const int64_t e = blk64(r, c, k);
+        *reinterpret_cast<uint2 *>(hi + e) = *reinterpret_cast<uint2 *>(h);
+        *reinterpret_cast<uint2 *>(lo + e) = *reinterpret_cast<uint2 *>(l);
+    }
+}
+
 // Exact dequantization of W [n][k] (ggml blocks) -> hi, lo bf16, 64x64-blocked.
 template <int T>
 __global__ void k_split_weight(const uint8_t *w, int64_t n, int k, __nv_bfloat16 *hi, __nv_bfloat16 *lo) {
@@ -570,6 +624,17 @@ cudaError_t split_act_norm_launch(const float *x, int ldx, int m, int k, const f
     if (m <= 0) return cudaSuccess;
     if (k % 4 || ldx % 4 || !norm_w || ((uintptr_t)x & 15) || ((uintptr_t)norm_w & 15)) return cudaErrorInvalidValue;
     cudaError_t e = launch_pdl(k_split_act_norm, dim3(m), dim3(256), 0, st, x, ldx, k, norm_w, eps,
+                               static_cast<__nv_bfloat16 *>(hi), static_cast<__nv_bfloat16 *>(lo));
+    if (e != cudaSuccess) return e;
+    return launched(1);
+}
+
+cudaError_t split_act_reduce_norm_launch(const float *ws, int ks, int m, float *x, int k, const float *norm_w,
+                                         float eps, void *hi, void *lo, cudaStream_t st) {
+    if (m <= 0) return cudaSuccess;
+    if (ks < 1 || k % 4 || !norm_w || ((uintptr_t)x & 15) || ((uintptr_t)ws & 15) || ((uintptr_t)norm_w & 15))
+        return cudaErrorInvalidValue;
+    cudaError_t e = launch_pdl(k_split_act_reduce_norm, dim3(m), dim3(256), 0, st, ws, ks, m, x, k, norm_w, eps,
                                static_cast<__nv_bfloat16 *>(hi), static_cast<__nv_bfloat16 *>(lo));
     if (e != cudaSuccess) return e;
     return launched(1);

@@ -478,7 +478,8 @@ static cudaError_t dq_inst(const DqArgs &a, dim3 grid, size_t smem, cudaStream_t
 // Same interface as mma_gemm_launch, the weights given as GGUF rows
 // (MmaGemmSeg::w / w2 / wtype); their types are one dq_type or {Q4_K, Q6_K}.
 cudaError_t mma_dq_launch(const MmaGemmSeg *segs, int nseg, const TensorMap *x_hi, const TensorMap *x_lo, int m, int k,
-                          cudaStream_t st, float *ws, size_t ws_floats) {
+                          cudaStream_t st, float *ws, size_t ws_floats, int *defer_ks) {
+    if (defer_ks) *defer_ks = 0;
     if (nseg < 1 || nseg > DQ_MAX_SEG || m <= 0 || k % DKC) return cudaErrorInvalidValue;
     int ta = segs[0].wtype, tb = segs[0].wtype;
     for (int i = 0; i < nseg; i++) {
@@ -567,6 +568,10 @@ cudaError_t mma_dq_launch(const MmaGemmSeg *segs, int nseg, const TensorMap *x_h
         }
     }
     if (e != cudaSuccess) return e;
+    if (a.ksplit > 1 && defer_ks) {
+        *defer_ks = a.ksplit;  // the caller reduces
+        return launched(1);
+    }
     if (a.ksplit > 1) {
         e = split_reduce_launch(ws, a.ksplit, m, (int)segs[0].n, segs[0].y, segs[0].ldy, segs[0].epi, segs[0].bias,
                                 segs[0].yrow, st);

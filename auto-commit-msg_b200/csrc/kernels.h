@@ -113,6 +113,10 @@ bool bf16_map(TensorMap *map, const void *base, int64_t rows, int64_t k);
 inline int64_t rows64(int64_t rows) { return (rows + 63) / 64 * 64; }
 // fp32 [m][ldx] -> bf16 hi, lo (blocked)
 cudaError_t split_act_launch(const float *x, int ldx, int m, int k, void *hi, void *lo, cudaStream_t st);
+// x[m][k] += the ks partial sums of ws (a deferred split-K reduce, EPI_ADD),
+// then RMSNorm and split of the rows, in one launch
+cudaError_t split_act_reduce_norm_launch(const float *ws, int ks, int m, float *x, int k, const float *norm_w,
+                                         float eps, void *hi, void *lo, cudaStream_t st);
 // RMSNorm of each row (weight norm_w) and its split in one launch
 cudaError_t split_act_norm_launch(const float *x, int ldx, int m, int k, const float *norm_w, float eps, void *hi,
                                   void *lo, cudaStream_t st);
@@ -159,8 +163,10 @@ cudaError_t mma_gemm_batched_launch(const MmaGemmSeg *segs, int nseg, const Tens
 // the segments' w / w2 / wtype (one quantized type, or Q4_K with Q6_K), K a
 // multiple of 256; otherwise as mma_gemm_launch.
 bool dq_type(int t);
+// defer_ks: when the launch splits K, leave the reduce to the caller and
+// report the slice count (0: no split, the outputs are written).
 cudaError_t mma_dq_launch(const MmaGemmSeg *segs, int nseg, const TensorMap *x_hi, const TensorMap *x_lo, int m, int k,
-                          cudaStream_t st, float *ws = nullptr, size_t ws_floats = 0);
+                          cudaStream_t st, float *ws = nullptr, size_t ws_floats = 0, int *defer_ks = nullptr);
 // Split-K epilogue: y[tok][n] (epi)= bias[n] + the ks partial sums of ws, in order.
 cudaError_t split_reduce_launch(const float *ws, int ks, int m, int n, float *y, int ldy, int epi, const float *bias,
                                 const int32_t *yrow, cudaStream_t st);
