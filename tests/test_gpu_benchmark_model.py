@@ -6,7 +6,7 @@ teacher-forced decode steps -- the shape, positions and kernels bench.py
 times (batch-1 decode GEMVs, decode attention over positions 389-452, the
 151936-row lm_head).
 
-Gates (north_star): every step's logits within 1e-3 relative L2 of the
+Gates (the parity bar of this workload): every step's logits within 1e-3 relative L2 of the
 oracle's fp32 path (internal/infer/model.go:317-442), and at least 99%
 greedy top-1 agreement.  A step whose oracle top-1 / top-2 margin is below
 twice the step's largest absolute logit difference counts as a tie: within

@@ -4,7 +4,7 @@ head_dim 64, interleaved rope, llama3 scaling) models with seeded random-init
 weights, at the prompt lengths of their workloads: 944 tokens, and 1500
 tokens (prefill chunks 1024 + 476, sampler.go:116).
 
-Gate (north_star): logits within 1e-3 relative L2 of the oracle's fp32 path
+Gate: logits within 1e-3 relative L2 of the oracle's fp32 path
 and greedy top-1 agreement, on the prefill and on teacher-forced decode
 steps.  Decoding the Llama model to its full 2048-position context is
 checked through size-independent properties: every step succeeds, the
